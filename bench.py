@@ -1,0 +1,364 @@
+"""Benchmark of the 32K Qwen2.5-7B-shape block-sparse prefill attention layer (config 2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--method mean_native] [--alpha 0.08] [--variant iid|structured]
+
+One step = one attention layer (route -> exact -> mean + merge) over B=1, L=32768,
+H=28, Hkv=4, d=128 synthetic inputs (N(0,1) + RoPE theta 1e6 + 32 needles) already
+resident in HBM; Q (235 MB) is larger than L2, so no flush is needed between steps.
+``value`` is whole-job effective TFLOP/s = 4 d x exact token pairs (kernels.py:339-350)
+over the max-over-ranks step time. With N GPUs (torchrun) the layer's independent work
+units — (KV group, query-tile range) — are split across ranks with no collective in the
+data path (strong scaling). ``--impl reference`` times the reference algorithm's CPU
+restatement (oracle/) on this host's cores on a bounded sample of the same layer.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SHAPE = dict(batch=1, length=32768, heads=28, kv_heads=4, head_dim=128)
+SCALE = 128 ** -0.5
+METRIC = "effective TFLOP/s of the 32K Qwen2.5-7B-shape prefill attention layer"
+WORKLOAD = ("config 2: one attention layer, B=1 L=32768 H=28 Hkv=4 d=128 bf16, synthetic N(0,1) Q/K/V + "
+            "RoPE(theta 1e6) + 32 needles")
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--method", default="mean_native")
+    ap.add_argument("--alpha", type=float, default=0.08)
+    ap.add_argument("--variant", default="iid", choices=["iid", "structured"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        data = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return data["bf16_tflops"], data.get("bf16_tflops_sustained"), data["hbm_gbs"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def inputs(variant, device):
+    from exp3_b200 import synthetic
+    kw = {"structured_sigma": 0.5} if variant == "structured" else {}
+    return synthetic.config_inputs("c2", seed=0, device=device, **kw)
+
+
+def partition(rank, world, kv_heads, blocks):
+    """Rank's (kv_range, tile_range): KV groups first, then causal-work-balanced tile ranges."""
+    if world <= kv_heads:
+        per = kv_heads // world
+        return (rank * per, (rank + 1) * per), (0, blocks)
+    parts = world // kv_heads
+    kv = rank // parts
+    j = rank % parts
+    # tile t costs ~ (t + 1): cut where the cumulative causal work reaches j / parts
+    cut = lambda i: min(blocks, int(round(blocks * math.sqrt(i / parts))))
+    return (kv, kv + 1), (cut(j), cut(j + 1))
+
+
+def exact_pairs(selected, length, kv_range, tile_range, group, block=128):
+    """4 d x pairs numerator (kernels.py:339-350) over the rank's heads and tiles."""
+    blocks = selected.shape[1]
+    counts = torch.full((blocks,), block, dtype=torch.int64, device=selected.device)
+    counts[-1] = length - (blocks - 1) * block
+    q_ids = torch.arange(blocks, device=selected.device).view(blocks, 1)
+    k_ids = torch.arange(blocks, device=selected.device).view(1, blocks)
+    weights = torch.where(k_ids < q_ids, counts.view(-1, 1) * counts.view(1, -1),
+                          torch.where(k_ids == q_ids, (counts * (counts + 1) // 2).view(-1, 1), 0))
+    h0, h1 = kv_range[0] * group, kv_range[1] * group
+    t0, t1 = tile_range
+    sub = selected[:, t0:t1, :, h0:h1].to(torch.int64)
+    return int((sub * weights[t0:t1].view(1, t1 - t0, blocks, 1)).sum())
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return None
+        mhz = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            for name, val in zip(names, r[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": float(self.rows[0][2]) if self.rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def cpu_sample_tiles(blocks):
+    # a late, a middle and an early tile: the routing + exact + mean work of the whole layer
+    # is ~ sum_t (t + 1); these three cover the range of per-tile costs.
+    return [blocks - 1, blocks // 2, blocks // 8]
+
+
+def cpu_baseline(method, alpha, q, k, v, budget_s=15.0):
+    """Times the oracle (the reference algorithm restated on the CPU, fp32 like the reference's
+    torch code) with all host threads on a bounded sample of query tiles."""
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    blocks = oracle.num_blocks(q.shape[1])
+    tiles = cpu_sample_tiles(blocks)
+    flops = 0
+    elapsed = 0.0
+    runs = 0
+    while runs == 0 or (elapsed < budget_s and runs < 20):
+        t0 = time.perf_counter()
+        outs, sel, _ = oracle.prefill_attention_tiles(method, q, k, v, SCALE, alpha, tiles=tiles)
+        elapsed += time.perf_counter() - t0
+        flops += 4 * 128 * oracle.exact_token_pairs(sel, q.shape[1])
+        runs += 1
+    return {"value": flops / elapsed / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"query tiles {tiles} of the 32K layer, all 28 heads, {runs} pass(es), "
+                      f"{elapsed:.1f} s, oracle/ fp32 torch on {threads} threads"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    q, k, v = inputs(args.variant, "cpu")
+    for _ in range(args.warmup):
+        cpu_baseline(args.method, args.alpha, q, k, v, budget_s=0.0)
+    values = [cpu_baseline(args.method, args.alpha, q, k, v, budget_s=0.0) for _ in range(args.steps)]
+    value = statistics.median(v["value"] for v in values)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "method": args.method, "alpha": args.alpha, "variant": args.variant},
+            "cpu_baseline": {**values[0], "value": value},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.warmup < 3:
+        raise SystemExit("at least 3 warm-up steps")
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch.distributed as dist
+    from exp3_b200 import ops
+    from exp3_b200._capi import STAGE_EXACT, STAGE_MEAN, STAGE_ROUTE
+    from exp3_b200.attention import AttentionBackend
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    b, length, heads, kv_heads, d = (SHAPE[x] for x in ("batch", "length", "heads", "kv_heads", "head_dim"))
+    group = heads // kv_heads
+    blocks = length // 128
+    q, k, v = inputs(args.variant, dev)
+    kv_range, tile_range = partition(rank, world, kv_heads, blocks)
+    method, alpha = args.method, args.alpha
+    nbytes = ops.workspace_bytes(method, b, length, heads, kv_heads)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = torch.empty(b, length, heads, d, dtype=torch.bfloat16, device=dev)
+
+    # Selected work of this rank (routing of the full layer, untimed).
+    ops.prefill_attention(q, k, v, method, alpha, SCALE, out=out, ws=ws, stages=STAGE_ROUTE)
+    selected, _, _ = ops.export_routing(method, b, length, heads, kv_heads, ws=ws, device=dev)
+    pairs = exact_pairs(selected, length, kv_range, tile_range, group)
+    all_pairs = exact_pairs(selected, length, (0, kv_heads), (0, blocks), group)
+    density = float(selected.sum()) / (b * heads * blocks * (blocks + 1) / 2)
+    flops = 4 * d * pairs
+    total_flops = 4 * d * all_pairs
+    del selected
+
+    def step(events=None):
+        common = dict(out=out, ws=ws, kv_range=kv_range, tile_range=tile_range)
+        if events is None:
+            ops.prefill_attention(q, k, v, method, alpha, SCALE, **common)
+            return
+        events[0].record()
+        ops.prefill_attention(q, k, v, method, alpha, SCALE, stages=STAGE_ROUTE, **common)
+        events[1].record()
+        ops.prefill_attention(q, k, v, method, alpha, SCALE, stages=STAGE_EXACT, **common)
+        events[2].record()
+        ops.prefill_attention(q, k, v, method, alpha, SCALE, stages=STAGE_MEAN, **common)
+        events[3].record()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(ev[i])
+        end.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_total = start.elapsed_time(end)
+    route_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    exact_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    mean_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in ev)
+    ms_step = ms_total / args.steps
+    if world > 1:
+        t = torch.tensor([ms_step], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step = float(t)
+
+    # End to end through the public API (AttentionBackend.forward, the attention.py call site)
+    # with pinned host buffers: H2D of this rank's Q/K/V, the layer, D2H of its output rows.
+    h0, h1 = kv_range[0] * group, kv_range[1] * group
+    t0, t1 = tile_range
+    q_h = q[:, :, h0:h1].contiguous().cpu().pin_memory()
+    k_h = k[:, :, kv_range[0]:kv_range[1]].contiguous().cpu().pin_memory()
+    v_h = v[:, :, kv_range[0]:kv_range[1]].contiguous().cpu().pin_memory()
+    o_h = torch.empty(b, (t1 - t0) * 128, h1 - h0, d, dtype=torch.bfloat16).pin_memory()
+    qd, kd, vd = (torch.empty_like(x, device=dev) for x in (q_h, k_h, v_h))
+    backend = AttentionBackend(alpha=alpha)
+    backend.configure(method)
+
+    class Layer:
+        layer_idx = 0
+
+    def e2e_step():
+        qd.copy_(q_h, non_blocking=True)
+        kd.copy_(k_h, non_blocking=True)
+        vd.copy_(v_h, non_blocking=True)
+        if tile_range == (0, blocks):
+            o, _ = backend.forward(Layer(), qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2), None, SCALE)
+        else:  # a tile shard: the same fused op with this rank's tile range
+            o = ops.prefill_attention(qd, kd, vd, method, alpha, SCALE, tile_range=tile_range)
+        o_h.copy_(o[:, t0 * 128:t1 * 128], non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e2.record()
+    torch.cuda.synchronize()
+    e2e_ms = s2.elapsed_time(e2) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t)
+    h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h))
+    d2h = o_h.numel() * o_h.element_size()
+    if world > 1:
+        counts = torch.tensor([float(h2d), float(d2h)], device=dev)
+        dist.all_reduce(counts)
+        h2d, d2h = int(counts[0]), int(counts[1])
+
+    peak, peak_sus, hbm, peak_kind = peaks()
+    achieved = flops / (exact_ms * 1e-3) / 1e12
+    traffic = None
+    traffic_file = ROOT / "profiles" / "exact_attention_traffic.json"
+    if traffic_file.exists():
+        try:
+            traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch_c2")
+        except ValueError:
+            traffic = None
+    launches_per_step = {"dense": 2, "fp_v1": 3}.get(method, 4)
+    if method in ("mean_balanced", "cgf_mean", "dispersion_mean") and alpha == 0:
+        launches_per_step = 4
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            qc, kc, vc = q.cpu(), k.cpu(), v.cpu()
+            cpu = cpu_baseline(method, alpha, qc, kc, vc)
+        line = {
+            "metric": METRIC, "value": total_flops / (ms_step * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "method": method, "alpha": alpha, "variant": args.variant,
+                       "ms_per_layer": ms_step, "density": density, "exact_token_pairs": all_pairs,
+                       "l2": "no flush: Q (235 MB) and O are larger than the 126 MB L2",
+                       "parallelism": f"{world} rank(s): (KV group x query-tile range) shards, no collective",
+                       "stage_ms_rank0": {"route": route_ms, "exact": exact_ms, "mean_merge": mean_ms}},
+            "roofline": {"bound": "tensor", "kernel": "exact attention (sparse FA)", "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_kind": f"{peak_kind} burst bf16", "frac_of_sustained":
+                             achieved / peak_sus if peak_sus else None, "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,48 @@
+// Parameter blocks and launchers of the exact-path and mean-tail kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace fpx {
+
+enum ExactMode { kExactLists = 0, kExactRefLayout = 1, kExactDense = 2 };
+
+struct ExactParams {
+  const __nv_bfloat16 *q, *k, *v;
+  int64_t q_sb, q_sl, q_sh, k_sb, k_sl, k_sh, v_sb, v_sl, v_sh;
+  __nv_bfloat16 *out;
+  int64_t o_sb, o_sl, o_sh;
+  float *lse;                       // [B][L][H] or null
+  int L, nb, H, group, head_begin, tile_begin;
+  float scale_log2;
+  RouteView route;                  // kExactLists
+  const int64_t *ref_indices;       // kExactRefLayout: [B][nb][nb][H]
+  const int32_t *ref_counts;        //                  [B][nb][H]
+};
+
+int launch_exact_mma(const ExactParams &p, int mode, int tiles, int heads, int B, cudaStream_t s);
+
+enum MeanMode { kMeanMergeInPlace = 0, kMeanStandalone = 1 };
+
+struct MeanParams {
+  const __nv_bfloat16 *q;
+  int64_t q_sb, q_sl, q_sh;
+  const float *mean_k, *mean_v;     // [B][nb][Hkv][d]
+  int L, nb, H, Hkv, group, head_begin, tile_begin;
+  float scale;
+  RouteView route;                  // kMeanMergeInPlace: tail bits
+  const uint8_t *mask;              // kMeanStandalone: selected [B][nb][nb][H]
+  // kMeanMergeInPlace: exact output (bf16, merged in place) and its LSE (updated in place)
+  __nv_bfloat16 *out;
+  int64_t o_sb, o_sl, o_sh;
+  float *lse;
+  // kMeanStandalone: fp32 mean-tail output [B][L][H][d] and LSE [B][L][H]
+  float *mean_out, *mean_lse;
+};
+
+int launch_mean_tail(const MeanParams &p, int mode, int tiles, int heads, int B, cudaStream_t s);
+int launch_merge(const __nv_bfloat16 *exact_out, const float *exact_lse, const float *mean_out,
+                 const float *mean_lse, int64_t rows, __nv_bfloat16 *out, float *lse,
+                 cudaStream_t s);
+
+}  // namespace fpx

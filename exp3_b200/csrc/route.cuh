@@ -1,0 +1,65 @@
+// Parameter blocks and launchers of the routing kernels (route.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace fpx {
+
+struct StatsParams {
+  const __nv_bfloat16 *k, *v;
+  int64_t k_sb, k_sl, k_sh, v_sb, v_sl, v_sh;
+  int L, nb, Hkv, kv_begin;
+  __nv_bfloat16 *mean_bf16;                      // [B][nb][Hkv][d] (V1 block mean)
+  float *mean_k, *mean_v, *var_k, *sigma_v;      // fp32 descriptors
+  int32_t *counts;                               // [nb] or null
+};
+
+// What the selection epilogue needs (compact lists are written when route.lists != null).
+struct SelectArgs {
+  RouteView route;
+  int nb, H, sink, window, last_full;
+  float alpha;
+  bool all_causal;
+};
+
+struct V1Params {
+  const __nv_bfloat16 *q;
+  int64_t q_sb, q_sl, q_sh;
+  const __nv_bfloat16 *mean_k;  // [B][nb][Hkv][d]
+  int L, nb, H, Hkv, group, head_begin, tile_begin;
+  float scale_log2;             // fp32(scale) * fp32(log2 e), as the reference kernel forms it
+  float *scores;                // reference layout [B][nb][nb][H], or null
+  SelectArgs sel;
+};
+
+struct SelParams {
+  const __nv_bfloat16 *q;
+  int64_t q_sb, q_sl, q_sh;
+  const float *mean_k, *var_k, *sigma_v;
+  int L, nb, H, Hkv, group, head_begin, tile_begin;
+  float scale, scale2;          // fp32(scale), fp32(scale * scale)
+  float *scores;
+  SelectArgs sel;
+};
+
+struct ColumnSelectParams {
+  const float *scores;
+  int nb, H, sink, window, last_full, min_budget, mode;
+  float alpha;
+  bool all_causal;
+  int64_t *indices;
+  int32_t *counts;
+  uint8_t *mask;
+};
+
+int launch_block_stats(const StatsParams &p, int blocks, int kv_count, int B, bool bf16_mean,
+                       bool desc, cudaStream_t s);
+int launch_v1_route(const V1Params &p, int tiles, int heads, int B, cudaStream_t s);
+int launch_selector_route(const SelParams &p, int selector, int tiles, int heads, int B,
+                          cudaStream_t s);
+int launch_causal_route(const RouteView &r, int H, int head_begin, int heads, int tile_begin,
+                        int tiles, int B, cudaStream_t s);
+int launch_export_routing(const RouteView &r, int H, int B, uint8_t *mask, int64_t *indices,
+                          int32_t *counts, cudaStream_t s);
+
+}  // namespace fpx

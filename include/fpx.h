@@ -1,0 +1,195 @@
+/*
+ * fpx — B200-native (sm_100a) block-sparse prefill attention with block-mean K/V correction.
+ *
+ * The C ABI of libfpx.so. Every entry point takes raw device pointers, sizes and
+ * element strides, launches on the given CUDA stream, never allocates device
+ * memory, never synchronises, and returns an fpx_status (0 = ok, negative =
+ * error; fpx_status_string() names it). Where a reference op mutates nothing
+ * and returns fresh tensors, the caller passes the output buffers.
+ *
+ * Layouts follow the reference's public entry points (exp3 attention.py:211-213
+ * makes them contiguous): q [B, L, H, d], k / v [B, L, Hkv, d] bf16 with the
+ * last dimension contiguous and the other three strides given in elements;
+ * block scores [B, nb, nb, H] fp32 (query block, key block, head); block index
+ * lists [B, nb, nb, H] int64 ascending with sentinel nb; counts [B, nb, H] int32;
+ * masks [B, nb, nb, H] uint8 (0/1, torch.bool storage). nb = ceil(L / block).
+ * Only block = 128 and d = 128 are compiled; other values return
+ * FPX_ERR_UNSUPPORTED.
+ *
+ * Reference file:line citations are to the exp3 tree; "upstream" means
+ * upstream/flashprefill_native_forward.py.
+ */
+#ifndef FPX_H_
+#define FPX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *fpx_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+enum fpx_status {
+  FPX_OK = 0,
+  FPX_ERR_INVALID = -1,     /* bad argument (null pointer, non-positive size, unknown enum) */
+  FPX_ERR_SHAPE = -2,       /* inconsistent shapes (H not a multiple of Hkv, ranges out of bounds) */
+  FPX_ERR_UNSUPPORTED = -3, /* head_dim / block size / method not compiled */
+  FPX_ERR_CUDA = -4,        /* a CUDA launch failed; cudaGetLastError() has the cause */
+  FPX_ERR_WORKSPACE = -5,   /* workspace too small or misaligned (256 B) */
+  FPX_ERR_TIMEOUT = -6      /* a bounded device-side wait gave up (see fpx_device_error) */
+};
+
+/* attention.py:15-24 METHODS, in order. */
+enum fpx_method {
+  FPX_METHOD_DENSE = 0,
+  FPX_METHOD_FP_V1 = 1,
+  FPX_METHOD_MEAN_NATIVE = 2,
+  FPX_METHOD_MEAN_BALANCED = 3,
+  FPX_METHOD_CGF_MEAN = 4,
+  FPX_METHOD_DISPERSION_MEAN = 5,
+  FPX_METHOD_FP_V1_RESCUE = 6,   /* not built: returns FPX_ERR_UNSUPPORTED */
+  FPX_METHOD_FP_V1_RESCUE_V2 = 7 /* not built: returns FPX_ERR_UNSUPPORTED */
+};
+
+/* Stage bits for fpx_prefill_attention (the profile stages of attention.py:66-75). */
+enum fpx_stage {
+  FPX_STAGE_ROUTE = 1, /* "descriptor" + "selector" + "indices" */
+  FPX_STAGE_EXACT = 2, /* "exact" */
+  FPX_STAGE_MEAN = 4,  /* "mean" + "merge" (fused) */
+  FPX_STAGE_ALL = 7
+};
+
+const char *fpx_status_string(int status);
+int fpx_version(void);
+
+/* ---- routing ------------------------------------------------------------------------ */
+
+/* upstream:420-442 block_mean_k (compute_mean_vector upstream:27-69): bf16 mean of the
+ * valid K rows of each (block, KV head) -> mean_k bf16 [B, nb, Hkv, d] contiguous.
+ * Sum order: fp32, rows in sequence; fp32 division by the row count; RNE to bf16. */
+int fpx_block_mean_k(const void *k, int64_t k_sb, int64_t k_sl, int64_t k_sh,
+                     int B, int L, int Hkv, int d, int block, void *mean_k, fpx_stream_t stream);
+
+/* kernels.py:22-46 block_descriptors: fp32 mean_k, mean_v, var_k [B, nb, Hkv, d],
+ * sigma_v [B, nb, Hkv], counts [nb] int32. */
+int fpx_block_descriptors(const void *k, int64_t k_sb, int64_t k_sl, int64_t k_sh,
+                          const void *v, int64_t v_sb, int64_t v_sl, int64_t v_sh,
+                          int B, int L, int Hkv, int d, int block,
+                          float *mean_k, float *mean_v, float *var_k, float *sigma_v,
+                          int32_t *counts, fpx_stream_t stream);
+
+/* upstream:445-475 v1_scores (compute_block_score upstream:89-175 + normalize_scores
+ * upstream:410-417): normalised V1 proxy scores [B, nb, nb, H] fp32 from bf16 mean_k. */
+int fpx_v1_scores(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                  const void *mean_k, int B, int L, int H, int Hkv, int d, int block,
+                  double scale, float *scores, fpx_stream_t stream);
+
+/* upstream:357-407 deal_output_score: keep = score >= alpha * max (or the min_budget
+ * top-k rule, upstream:368-371; ties broken towards the lower block id), OR the
+ * sink / window / last-blocks protection, AND causal -> ascending int64 indices with
+ * sentinel nb and int32 counts. */
+int fpx_deal_output_score(const float *scores, int B, int nb, int H, int sink, int window,
+                          double alpha, int last_full, int min_budget,
+                          int64_t *indices, int32_t *counts, fpx_stream_t stream);
+
+/* kernels.py:49-126 selector_scores for selector = FPX_METHOD_MEAN_BALANCED,
+ * FPX_METHOD_CGF_MEAN or FPX_METHOD_DISPERSION_MEAN -> [B, nb, nb, H] fp32. */
+int fpx_selector_scores(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                        const float *mean_k, const float *var_k, const float *sigma_v,
+                        const int32_t *counts, int B, int L, int H, int Hkv, int d, int block,
+                        int selector, double scale, float *scores, fpx_stream_t stream);
+
+/* kernels.py:129-151 protected_selection -> mask [B, nb, nb, H] uint8. */
+int fpx_protected_selection(const float *scores, int B, int nb, int H, double alpha, int sink,
+                            int window, int last_full, uint8_t *selected, fpx_stream_t stream);
+
+/* kernels.py:154-160 indices_from_mask and kernels.py:163-176 mask_from_indices. */
+int fpx_indices_from_mask(const uint8_t *selected, int B, int nb, int H,
+                          int64_t *indices, int32_t *counts, fpx_stream_t stream);
+int fpx_mask_from_indices(const int64_t *indices, const int32_t *counts, int B, int nb, int H,
+                          uint8_t *selected, fpx_stream_t stream);
+
+/* kernels.py:328-407 selection_accounting, device part: counters[0] = exact token pairs,
+ * counters[1] = selected block entries, counters[2] = mean proxy entries (int64). */
+int fpx_selection_accounting(const uint8_t *selected, int B, int nb, int H, int L, int block,
+                             int64_t *counters, fpx_stream_t stream);
+
+/* ---- exact path, mean tail, merge ---------------------------------------------------- */
+
+/* upstream:478-521 exact_attention (_flash_forward upstream:215-354): block-sparse causal
+ * attention over the listed blocks -> out bf16 [B, L, H, d] contiguous, lse fp32 [B, L, H]
+ * natural log. */
+int fpx_exact_attention(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                        const void *k, int64_t k_sb, int64_t k_sl, int64_t k_sh,
+                        const void *v, int64_t v_sb, int64_t v_sl, int64_t v_sh,
+                        const int64_t *indices, const int32_t *counts,
+                        int B, int L, int H, int Hkv, int d, int block, double scale,
+                        void *out, float *lse, fpx_stream_t stream);
+
+/* kernels.py:179-230 mean_tail: unselected strictly-earlier blocks through fp32 block
+ * means (+ log count) -> out fp32 [B, L, H, d], lse fp32 [B, L, H] (-inf without tail). */
+int fpx_mean_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                  const float *mean_k, const float *mean_v, const int32_t *counts,
+                  const uint8_t *selected, int B, int L, int H, int Hkv, int d, int block,
+                  double scale, float *out, float *lse, fpx_stream_t stream);
+
+/* kernels.py:312-325 merge_exact_mean over rows = B * L * H rows of d: out (bf16, the
+ * exact output's dtype) and lse fp32. */
+int fpx_merge_exact_mean(const void *exact_out, const float *exact_lse, const float *mean_out,
+                         const float *mean_lse, int64_t rows, int d, void *out, float *lse,
+                         fpx_stream_t stream);
+
+/* ---- the fused prefill path (attention.py:210-333) ---------------------------------- */
+
+/* Device bytes of workspace fpx_prefill_attention needs (256-byte aligned). */
+size_t fpx_prefill_workspace_bytes(int method, int B, int L, int H, int Hkv, int d, int block);
+
+/* The prefill branch of AttentionBackend.forward (attention.py:210-333) for the KV heads
+ * [kv_begin, kv_end) and query tiles [tile_begin, tile_end) (pass 0, Hkv, 0, nb for all):
+ * route -> exact -> mean + merge. out bf16 with element strides (o_sb, o_sl, o_sh);
+ * lse fp32 [B, L, H] or NULL. `stages` (fpx_stage bits) runs a subset of the stages on
+ * the same workspace, so each can be timed; a later stage needs the earlier ones' output
+ * in the workspace. */
+int fpx_prefill_attention(int method, double alpha, int sink, int window, int last_full,
+                          const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                          const void *k, int64_t k_sb, int64_t k_sl, int64_t k_sh,
+                          const void *v, int64_t v_sb, int64_t v_sl, int64_t v_sh,
+                          int B, int L, int H, int Hkv, int d, int block, double scale,
+                          int kv_begin, int kv_end, int tile_begin, int tile_end,
+                          void *out, int64_t o_sb, int64_t o_sl, int64_t o_sh, float *lse,
+                          void *workspace, size_t workspace_bytes, int stages,
+                          fpx_stream_t stream);
+
+/* Copies the routing result of the last fpx_prefill_attention on this workspace (run over
+ * all KV heads and tiles) out in the reference's layouts: selected mask uint8
+ * [B, nb, nb, H] and, if non-NULL, ascending int64 indices [B, nb, nb, H] with sentinel nb
+ * and int32 counts [B, nb, H]. */
+int fpx_prefill_export_routing(int method, int B, int L, int H, int Hkv, int d, int block,
+                               const void *workspace, size_t workspace_bytes,
+                               uint8_t *selected, int64_t *indices, int32_t *counts,
+                               fpx_stream_t stream);
+
+/* ---- dense decode (attention.py:178-189) --------------------------------------------- */
+
+/* Device bytes of workspace fpx_decode_attention needs. */
+size_t fpx_decode_workspace_bytes(int B, int Lq, int H, int Hkv, int S, int d);
+
+/* The decode branch of AttentionBackend.forward (attention.py:178-189: q_len != k_len, so
+ * F.scaled_dot_product_attention(is_causal=False, enable_gqa=True)): every query row of
+ * q [B, Lq, H, d] attends to all S keys of k / v [B, S, Hkv, d] (strided views of HF's
+ * [B, Hkv, S, d] cache are fine) -> out bf16 with element strides, lse fp32 [B, Lq, H] or
+ * NULL. Split-K over the cache; H / Hkv <= 16. */
+int fpx_decode_attention(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                         const void *k, int64_t k_sb, int64_t k_sl, int64_t k_sh,
+                         const void *v, int64_t v_sb, int64_t v_sl, int64_t v_sh,
+                         int B, int Lq, int S, int H, int Hkv, int d, double scale,
+                         void *out, int64_t o_sb, int64_t o_sl, int64_t o_sh, float *lse,
+                         void *workspace, size_t workspace_bytes, fpx_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FPX_H_ */
