@@ -28,6 +28,8 @@ S3 = [c_i64, c_i64, c_i64]
 SIGNATURES = {
     "fpx_status_string": ([c_int], ctypes.c_char_p),
     "fpx_version": ([], c_int),
+    "fpx_set_option": ([c_int, c_int], c_int),
+    "fpx_device_error": ([ctypes.POINTER(c_int), c_int], c_int),
     "fpx_block_mean_k": ([P, *S3, c_int, c_int, c_int, c_int, c_int, P, P], c_int),
     "fpx_block_descriptors": ([P, *S3, P, *S3, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P], c_int),
     "fpx_v1_scores": ([P, *S3, P, c_int, c_int, c_int, c_int, c_int, c_int, c_double, P, P], c_int),

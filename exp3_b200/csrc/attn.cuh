@@ -21,6 +21,13 @@ struct ExactParams {
 };
 
 int launch_exact_mma(const ExactParams &p, int mode, int tiles, int heads, int B, cudaStream_t s);
+// tcgen05 / TMEM / TMA exact kernel over internal lists (kExactLists).
+int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s);
+
+// Process-wide options (fpx_set_option): which exact kernel the fused path runs.
+enum Option { kOptExactKernel = 1 };
+enum ExactKernel { kExactKernelTcgen05 = 0, kExactKernelMmaSync = 1 };
+int get_option(int key);
 
 enum MeanMode { kMeanMergeInPlace = 0, kMeanStandalone = 1 };
 

@@ -1,0 +1,342 @@
+// Exact block-sparse causal attention on the 5th-generation tensor core (tcgen05 + TMEM + TMA).
+//
+// Reference semantics: upstream/flashprefill_native_forward.py:215-354 (_flash_forward) —
+// for query tile t (128 rows) of head h, attend over the tile's selected 128-key blocks in
+// ascending order with an online softmax in exp2 units, causal mask on the diagonal block,
+// P rounded to bf16 before P.V, bf16 output and natural-log LSE.
+//
+// One CTA per (batch, head, query tile), 192 threads in three roles:
+//   warp 0      TMA producer: Q once, then K and V of each selected block into a 2-stage ring;
+//   warp 1      MMA issuer (one elected lane): S = Q K^T into a double-buffered TMEM S, then
+//               O += P V into TMEM O once the softmax has published P;
+//   warps 2..5  softmax (thread = query row = TMEM lane): read S from TMEM, mask, online
+//               softmax, rescale O in TMEM when the row max grows, write P (bf16) into a
+//               swizzled shared tile, and finally normalise O and store it with TMA.
+// TMEM: columns [0,128) S0, [128,256) S1, [256,384) O (fp32, 128 lanes). Every mbarrier wait
+// is bounded; a wait that gives up flags the CTA, the roles drain and exit, and the host sees
+// FPX_ERR_TIMEOUT through fpx_device_error().
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "attn.cuh"
+#include "tc.cuh"
+
+namespace fpx {
+
+__device__ int g_device_error;  // 0 = ok; 1 = a bounded wait in a tcgen05 kernel gave up
+
+namespace {
+
+using namespace tc;
+
+constexpr int kStages = 2;
+constexpr int kThreads = 192;
+constexpr uint32_t kHalf = 128 * 128;  // 128 rows x 64 bf16 (one SW128 half tile)
+constexpr uint32_t kTile = 2 * kHalf;  // 128 x 128 bf16
+constexpr uint32_t kIdescQK = idesc_bf16(128, 128, false);
+constexpr uint32_t kIdescPV = idesc_bf16(128, 128, true);
+
+struct alignas(1024) Smem {
+  uint8_t q[kTile];
+  uint8_t k[kStages][kTile];
+  uint8_t v[kStages][kTile];
+  uint8_t p[kTile];
+  uint64_t q_full, k_full[kStages], v_full[kStages], kv_empty[kStages];
+  uint64_t s_full[2], s_empty[2], p_full, o_done, drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// K-major SW128 operand (Q, K, P) at K offset 16*kk: halves of 64 columns sit kHalf apart,
+// 16 columns = 32 bytes inside a half.
+FPX_INLINE uint64_t desc_kmajor(const uint8_t *tile, int kk) {
+  const uint32_t a = smem_u32(tile) + (kk >> 2) * kHalf + (kk & 3) * 32;
+  return smem_desc_sw128(a, 16, 1024);
+}
+// MN-major SW128 V operand at key offset 16*kk: 16 keys = 16 rows of 128 bytes.
+FPX_INLINE uint64_t desc_v(const uint8_t *tile, int kk) {
+  return smem_desc_sw128(smem_u32(tile) + kk * 2048, kHalf, 1024);
+}
+
+// Byte offset of (row, col) inside a 128 x 128 bf16 SW128 K-major tile.
+FPX_INLINE uint32_t sw128_offset(int row, int col) {
+  const int half = col >> 6, chunk = (col & 63) >> 3;
+  return half * kHalf + row * 128 + ((chunk ^ (row & 7)) << 4) + ((col & 7) << 1);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+    exact_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                    ExactParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  Smem &sh = *reinterpret_cast<Smem *>(smem_raw + pad);
+  volatile int *abort = &sh.abort;
+
+  const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);
+  const int h = p.head_begin + blockIdx.y;
+  const int b = blockIdx.z;
+  const int kvh = h / p.group;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rrow = p.route.row(b, h, t, p.H);
+  const int count = p.route.counts[rrow];
+  const int32_t *list = p.route.lists + rrow * p.route.nb;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sh.q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sh.k_full[s], 1);
+      mbar_init(&sh.v_full[s], 1);
+      mbar_init(&sh.kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sh.s_full[s], 1);
+      mbar_init(&sh.s_empty[s], 128);
+    }
+    mbar_init(&sh.p_full, 128);
+    mbar_init(&sh.o_done, 1);
+    mbar_init(&sh.drain, 1);
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sh.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    int issued[kStages] = {0, 0};
+    if (count > 0) {
+      if (lane == 0) {
+        mbar_expect_tx(&sh.q_full, kTile);
+        tma_load_4d(sh.q, &tm_q, &sh.q_full, 0, h, t * 128, b);
+        tma_load_4d(sh.q + kHalf, &tm_q, &sh.q_full, 64, h, t * 128, b);
+      }
+      for (int j = 0; j < count; ++j) {
+        const int s = j % kStages, n = j / kStages;
+        if (n > 0 && !mbar_wait(&sh.kv_empty[s], (n - 1) & 1, abort)) break;
+        const int blk = list[j];
+        if (lane == 0) {
+          mbar_expect_tx(&sh.k_full[s], kTile);
+          tma_load_4d(sh.k[s], &tm_k, &sh.k_full[s], 0, kvh, blk * 128, b);
+          tma_load_4d(sh.k[s] + kHalf, &tm_k, &sh.k_full[s], 64, kvh, blk * 128, b);
+          mbar_expect_tx(&sh.v_full[s], kTile);
+          tma_load_4d(sh.v[s], &tm_v, &sh.v_full[s], 0, kvh, blk * 128, b);
+          tma_load_4d(sh.v[s] + kHalf, &tm_v, &sh.v_full[s], 64, kvh, blk * 128, b);
+        }
+        issued[s] = n + 1;
+      }
+      __syncwarp();
+      if (*abort) {  // drain copies still in flight before the CTA's shared memory goes away
+        int never = 0;
+        mbar_wait(&sh.q_full, 0, &never);
+        for (int s = 0; s < kStages; ++s)
+          if (issued[s] > 0) {
+            mbar_wait(&sh.k_full[s], (issued[s] - 1) & 1, &never);
+            mbar_wait(&sh.v_full[s], (issued[s] - 1) & 1, &never);
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (count > 0 && mbar_wait(&sh.q_full, 0, abort)) {
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i % kStages;
+        if (!mbar_wait(&sh.p_full, i & 1, abort)) return false;
+        if (!mbar_wait(&sh.v_full[s], (i / kStages) & 1, abort)) return false;
+        tc_fence_after();
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ss(tmem + 256, desc_kmajor(sh.p, kk), desc_v(sh.v[s], kk), kIdescPV, (i > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&sh.kv_empty[s]);
+          tc_commit(&sh.o_done);
+        }
+        __syncwarp();
+        return true;
+      };
+      bool ok = true;
+      for (int j = 0; j < count && ok; ++j) {
+        const int s = j % kStages, sb = j & 1;
+        if (!mbar_wait(&sh.k_full[s], (j / kStages) & 1, abort)) break;
+        if (j >= 2 && !mbar_wait(&sh.s_empty[sb], ((j >> 1) - 1) & 1, abort)) break;
+        tc_fence_after();
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ss(tmem + sb * 128, desc_kmajor(sh.q, kk), desc_kmajor(sh.k[s], kk), kIdescQK, kk > 0 ? 1u : 0u);
+          tc_commit(&sh.s_full[sb]);
+        }
+        __syncwarp();
+        if (j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok && !*abort) issue_pv(count - 1);
+      if (*abort) {  // let every MMA this thread issued finish before TMEM is released
+        int never = 0;
+        if (lane == 0) tc_commit(&sh.drain);
+        __syncwarp();
+        mbar_wait(&sh.drain, 0, &never);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax warpgroup
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // query row in the tile == TMEM lane
+    const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
+    const int qrow = t * 128 + r;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < count && ok; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&sh.s_full[sb], (j >> 1) & 1, abort)) { ok = false; break; }
+      tc_fence_after();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + sb * 128 + 32 * c, *reinterpret_cast<float(*)[32]>(&s[32 * c]));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&sh.s_empty[sb]);
+      const int blk = list[j];
+      const int kmax = (blk == t) ? (r) : 127;  // diagonal block: key j <= row
+      float mx = m;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        const float x = (i <= kmax) ? s[i] * p.scale_log2 : -INFINITY;
+        s[i] = x;
+        mx = fmaxf(mx, x);
+      }
+      float rs = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float a = (mx == -INFINITY) ? 0.f : exp2f(s[2 * i] - mx);
+        const float c = (mx == -INFINITY) ? 0.f : exp2f(s[2 * i + 1] - mx);
+        rs += a + c;
+        pk[i] = pack_bf16(a, c);
+      }
+      const float corr = (m == -INFINITY) ? (mx == -INFINITY ? 1.f : 0.f) : exp2f(m - mx);
+      if (j > 0) {
+        if (!mbar_wait(&sh.o_done, (j - 1) & 1, abort)) { ok = false; break; }
+        if (corr != 1.f) {
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tmem_ld32(lane_addr + 256 + 32 * c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= corr;
+            tmem_st32(lane_addr + 256 + 32 * c, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      l = l * corr + rs;
+      m = mx;
+      // P row -> swizzled K-major tile (16-byte chunks).
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint4 v4 = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        *reinterpret_cast<uint4 *>(sh.p + sw128_offset(r, 8 * c)) = v4;
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(&sh.p_full);
+    }
+    // Epilogue: O / l -> bf16 -> swizzled tile (in the Q buffer) -> TMA store; LSE.
+    if (ok && count > 0) {
+      if (!mbar_wait(&sh.o_done, (count - 1) & 1, abort)) ok = false;
+    }
+    tc_fence_after();
+    const bool none = !(ok && count > 0) || m == -INFINITY;
+    const float inv = none ? 0.f : 1.f / l;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float o[32];
+      if (ok && count > 0) {
+        tmem_ld32(lane_addr + 256 + 32 * c, o);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 v4 = make_uint4(pack_bf16(o[8 * i] * inv, o[8 * i + 1] * inv), pack_bf16(o[8 * i + 2] * inv, o[8 * i + 3] * inv),
+                              pack_bf16(o[8 * i + 4] * inv, o[8 * i + 5] * inv), pack_bf16(o[8 * i + 6] * inv, o[8 * i + 7] * inv));
+        *reinterpret_cast<uint4 *>(sh.q + sw128_offset(r, 32 * c + 8 * i)) = v4;
+      }
+    }
+    if (p.lse && qrow < p.L) p.lse[((int64_t)b * p.L + qrow) * p.H + h] = none ? -INFINITY : m * kLn2 + logf(l);
+    fence_proxy_async();
+    named_sync(1, 128);
+    if (threadIdx.x == 64 && !*abort) {
+      tma_store_4d(&tm_o, sh.q, 0, h, t * 128, b);
+      tma_store_4d(&tm_o, sh.q + kHalf, 64, h, t * 128, b);
+      bulk_commit();
+      bulk_wait0();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && sh.abort) atomicExch(&g_device_error, 1);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+namespace {
+
+bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int64_t rows, int64_t batch, int64_t sh,
+               int64_t sl, int64_t sb) {
+  cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[3] = {(cuuint64_t)(sh * 2), (cuuint64_t)(sl * 2), (cuuint64_t)(sb * 2)};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  // A size-1 dimension may carry any stride; keep it a valid multiple of 16 bytes.
+  if (heads == 1) strides[0] = 16;
+  if (batch == 1) strides[2] = strides[1] * (cuuint64_t)rows;
+  return cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides,
+                                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+size_t exact_tc_smem() { return sizeof(Smem) + 1024; }
+
+int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s) {
+  if (tiles <= 0 || heads <= 0) return FPX_OK;
+  CUtensorMap tq, tk, tv, to;
+  if (!encode_4d(&tq, p.q, kHeadDim, p.H, L, B, p.q_sh, p.q_sl, p.q_sb) ||
+      !encode_4d(&tk, p.k, kHeadDim, Hkv, L, B, p.k_sh, p.k_sl, p.k_sb) ||
+      !encode_4d(&tv, p.v, kHeadDim, Hkv, L, B, p.v_sh, p.v_sl, p.v_sb) ||
+      !encode_4d(&to, p.out, kHeadDim, p.H, L, B, p.o_sh, p.o_sl, p.o_sb))
+    return FPX_ERR_INVALID;
+  const size_t smem = exact_tc_smem();
+  cudaFuncSetAttribute(exact_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  exact_tc_kernel<<<dim3(tiles, heads, B), kThreads, smem, s>>>(tq, tk, tv, to, p);
+  FPX_CHECK_LAUNCH();
+  return FPX_OK;
+}
+
+}  // namespace fpx
+
+extern "C" int fpx_device_error(int *code, int reset) {
+  if (!code) return FPX_ERR_INVALID;
+  if (cudaMemcpyFromSymbol(code, fpx::g_device_error, sizeof(int)) != cudaSuccess) return FPX_ERR_CUDA;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(fpx::g_device_error, &zero, sizeof(int)) != cudaSuccess) return FPX_ERR_CUDA;
+  }
+  return FPX_OK;
+}

@@ -71,6 +71,19 @@ extern "C" const char *fpx_status_string(int status) {
 
 extern "C" int fpx_version(void) { return 1; }
 
+namespace fpx {
+static int g_options[4] = {0, kExactKernelTcgen05, 0, 0};
+int get_option(int key) { return (key > 0 && key < 4) ? g_options[key] : 0; }
+}  // namespace fpx
+
+extern "C" int fpx_set_option(int key, int value) {
+  if (key == kOptExactKernel && (value == kExactKernelTcgen05 || value == kExactKernelMmaSync)) {
+    g_options[key] = value;
+    return FPX_OK;
+  }
+  return FPX_ERR_INVALID;
+}
+
 extern "C" size_t fpx_prefill_workspace_bytes(int method, int B, int L, int H, int Hkv, int d,
                                               int block) {
   (void)method; (void)d; (void)block;
@@ -168,7 +181,9 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     ep.head_begin = head_begin; ep.tile_begin = tile_begin;
     ep.scale_log2 = (float)scale * kLog2e;
     ep.route = rv;
-    rc = launch_exact_mma(ep, kExactLists, tiles, heads, B, s);
+    rc = get_option(kOptExactKernel) == kExactKernelMmaSync
+             ? launch_exact_mma(ep, kExactLists, tiles, heads, B, s)
+             : launch_exact_tc(ep, B, L, Hkv, tiles, heads, s);
     if (rc) return rc;
   }
   if ((stages & FPX_STAGE_MEAN) && is_mean_method(method)) {

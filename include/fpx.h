@@ -64,6 +64,14 @@ enum fpx_stage {
 const char *fpx_status_string(int status);
 int fpx_version(void);
 
+/* Process-wide options (no reference counterpart): key 1 selects the exact-attention kernel
+ * of fpx_prefill_attention — 0 = tcgen05/TMEM/TMA (default), 1 = mma.sync (cross-check). */
+int fpx_set_option(int key, int value);
+
+/* Reads (and with reset != 0 clears) the device error word set when a bounded wait inside a
+ * kernel gave up (1 = wait timeout); synchronous. No reference counterpart. */
+int fpx_device_error(int *code, int reset);
+
 /* ---- routing ------------------------------------------------------------------------ */
 
 /* upstream:420-442 block_mean_k (compute_mean_vector upstream:27-69): bf16 mean of the
