@@ -112,3 +112,17 @@ def strides3(t: torch.Tensor):
     if t.stride(-1) != 1:
         raise FpxError("the last dimension must be contiguous")
     return t.stride(0), t.stride(1), t.stride(2)
+
+
+def device_error(reset: bool = True) -> int:
+    """The device error word of libfpx (1 = a bounded wait in a kernel gave up); synchronises."""
+    code = ctypes.c_int(0)
+    rc = lib().fpx_device_error(ctypes.byref(code), 1 if reset else 0)
+    if rc != 0:
+        raise FpxError(f"fpx_device_error failed with status {rc}")
+    return code.value
+
+
+def set_exact_kernel(name: str) -> None:
+    """Selects the exact-attention kernel of the fused path: "tcgen05" (default) or "mma"."""
+    call("fpx_set_option", 1, {"tcgen05": 0, "mma": 1}[name])

@@ -60,7 +60,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     with concurrent.futures.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as pool:
         objs = list(pool.map(_compile, sources()))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stderr}")

@@ -82,7 +82,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kvh = h / p.group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t rrow = p.route.row(b, h, t, p.H);
-  const int count = p.route.counts[rrow];
+  // Once any CTA has given up on a wait, the rest skip their work (the launch is failed).
+  const int count = *reinterpret_cast<volatile int *>(&g_device_error) ? 0 : p.route.counts[rrow];
   const int32_t *list = p.route.lists + rrow * p.route.nb;
 
   if (threadIdx.x == 0) {
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int j = 0; j < count; ++j) {
         const int s = j % kStages, n = j / kStages;
-        if (n > 0 && !mbar_wait(&sh.kv_empty[s], (n - 1) & 1, abort)) break;
+        if (n > 0 && !mbar_wait_warp(&sh.kv_empty[s], (n - 1) & 1, abort)) break;
         const int blk = list[j];
         if (lane == 0) {
           mbar_expect_tx(&sh.k_full[s], kTile);
@@ -147,11 +148,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (count > 0 && mbar_wait(&sh.q_full, 0, abort)) {
+    if (count > 0 && mbar_wait_warp(&sh.q_full, 0, abort)) {
       auto issue_pv = [&](int i) -> bool {
         const int s = i % kStages;
-        if (!mbar_wait(&sh.p_full, i & 1, abort)) return false;
-        if (!mbar_wait(&sh.v_full[s], (i / kStages) & 1, abort)) return false;
+        if (!mbar_wait_warp(&sh.p_full, i & 1, abort)) return false;
+        if (!mbar_wait_warp(&sh.v_full[s], (i / kStages) & 1, abort)) return false;
         tc_fence_after();
         if (lane == 0) {
 #pragma unroll
@@ -166,8 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int j = 0; j < count && ok; ++j) {
         const int s = j % kStages, sb = j & 1;
-        if (!mbar_wait(&sh.k_full[s], (j / kStages) & 1, abort)) break;
-        if (j >= 2 && !mbar_wait(&sh.s_empty[sb], ((j >> 1) - 1) & 1, abort)) break;
+        if (!mbar_wait_warp(&sh.k_full[s], (j / kStages) & 1, abort)) break;
+        if (j >= 2 && !mbar_wait_warp(&sh.s_empty[sb], ((j >> 1) - 1) & 1, abort)) break;
         tc_fence_after();
         if (lane == 0) {
 #pragma unroll
@@ -196,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int j = 0; j < count && ok; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait(&sh.s_full[sb], (j >> 1) & 1, abort)) { ok = false; break; }
+      if (!mbar_wait_warp(&sh.s_full[sb], (j >> 1) & 1, abort)) { ok = false; break; }
       tc_fence_after();
       float s[128];
 #pragma unroll
@@ -224,8 +225,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float corr = (m == -INFINITY) ? (mx == -INFINITY ? 1.f : 0.f) : exp2f(m - mx);
       if (j > 0) {
-        if (!mbar_wait(&sh.o_done, (j - 1) & 1, abort)) { ok = false; break; }
-        if (corr != 1.f) {
+        if (!mbar_wait_warp(&sh.o_done, (j - 1) & 1, abort)) { ok = false; break; }
+        if (__any_sync(0xffffffffu, corr != 1.f)) {  // tcgen05.ld/st are warp-collective
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -253,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // Epilogue: O / l -> bf16 -> swizzled tile (in the Q buffer) -> TMA store; LSE.
     if (ok && count > 0) {
-      if (!mbar_wait(&sh.o_done, (count - 1) & 1, abort)) ok = false;
+      if (!mbar_wait_warp(&sh.o_done, (count - 1) & 1, abort)) ok = false;
     }
     tc_fence_after();
     const bool none = !(ok && count > 0) || m == -INFINITY;
@@ -296,6 +297,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 namespace {
 
+// cuTensorMapEncodeTiled, resolved through the runtime so the library loads without libcuda.
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(ptr);
+  }();
+  return fn;
+}
+
 bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int64_t rows, int64_t batch, int64_t sh,
                int64_t sl, int64_t sb) {
   cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)batch};
@@ -305,7 +323,9 @@ bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int
   // A size-1 dimension may carry any stride; keep it a valid multiple of 16 bytes.
   if (heads == 1) strides[0] = 16;
   if (batch == 1) strides[2] = strides[1] * (cuuint64_t)rows;
-  return cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides,
+  const EncodeTiledFn encode = encode_fn();
+  if (!encode) return false;
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides,
                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

@@ -51,6 +51,12 @@ FPX_INLINE bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
   }
   return true;
 }
+// Warp-uniform form: every lane of the warp agrees on the outcome, so warp-collective
+// tcgen05 instructions that follow are never reached by part of a warp.
+FPX_INLINE bool mbar_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort) {
+  const bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok);
+}
 FPX_INLINE void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 FPX_INLINE void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 

@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import oracle
-from exp3_b200 import decode, kernels, ops, synthetic, upstream
+from exp3_b200 import _capi, decode, kernels, ops, synthetic, upstream
 from exp3_b200.attention import AttentionBackend
 from golden_cases import SCALE, load, t
 
@@ -257,3 +257,20 @@ def test_config2_32k_properties_and_sampled_tiles():
     causal = 28 * 256 * 257 // 2
     assert int(cnt.sum()) == int(sel.sum()) <= causal
     assert math.isfinite(a.float().abs().max().item())
+
+
+def test_tcgen05_and_mma_exact_kernels_agree():
+    shape = synthetic.LayerShape(1, 2048, 28, 4)
+    q, k, v = cuda(*synthetic.attention_inputs(shape, seed=5, needles=3, structured_sigma=0.5))
+    results = []
+    try:
+        for which in ("mma", "tcgen05"):
+            _capi.set_exact_kernel(which)
+            lse = torch.empty(1, 2048, 28, device=DEV)
+            out = ops.prefill_attention(q, k, v, "mean_native", 0.08, SCALE, lse=lse)
+            results.append((out, lse))
+    finally:
+        _capi.set_exact_kernel("tcgen05")
+    torch.testing.assert_close(results[0][0].float(), results[1][0].float(), atol=O_TOL, rtol=0)
+    torch.testing.assert_close(results[0][1], results[1][1], atol=LSE_TOL, rtol=0)
+    assert _capi.device_error() == 0
