@@ -124,5 +124,6 @@ def device_error(reset: bool = True) -> int:
 
 
 def set_exact_kernel(name: str) -> None:
-    """Selects the exact-attention kernel of the fused path: "tcgen05" (default) or "mma"."""
-    call("fpx_set_option", 1, {"tcgen05": 0, "mma": 1}[name])
+    """Selects the exact-attention kernel of the fused path: "tcgen05" (two query tiles per CTA,
+    the default), "tcgen05_single" (one tile per CTA) or "mma" (mma.sync cross-check)."""
+    call("fpx_set_option", 1, {"tcgen05": 0, "mma": 1, "tcgen05_single": 2}[name])

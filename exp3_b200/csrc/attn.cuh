@@ -26,7 +26,7 @@ int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int 
 
 // Process-wide options (fpx_set_option): which exact kernel the fused path runs.
 enum Option { kOptExactKernel = 1 };
-enum ExactKernel { kExactKernelTcgen05 = 0, kExactKernelMmaSync = 1 };
+enum ExactKernel { kExactKernelTcgen05 = 0, kExactKernelMmaSync = 1, kExactKernelTcgen05Single = 2 };
 int get_option(int key);
 
 enum MeanMode { kMeanMergeInPlace = 0, kMeanStandalone = 1 };

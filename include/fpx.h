@@ -65,7 +65,8 @@ const char *fpx_status_string(int status);
 int fpx_version(void);
 
 /* Process-wide options (no reference counterpart): key 1 selects the exact-attention kernel
- * of fpx_prefill_attention — 0 = tcgen05/TMEM/TMA (default), 1 = mma.sync (cross-check). */
+ * of fpx_prefill_attention — 0 = tcgen05/TMEM/TMA with two query tiles per CTA (default),
+ * 1 = mma.sync (cross-check), 2 = tcgen05 with one query tile per CTA. */
 int fpx_set_option(int key, int value);
 
 /* Reads (and with reset != 0 clears) the device error word set when a bounded wait inside a
