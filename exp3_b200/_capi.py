@@ -51,6 +51,8 @@ SIGNATURES = {
     "fpx_decode_workspace_bytes": ([c_int, c_int, c_int, c_int, c_int, c_int], c_size),
     "fpx_decode_attention": ([P, *S3, P, *S3, P, *S3, c_int, c_int, c_int, c_int, c_int, c_int, c_double,
                               P, *S3, P, P, c_size, P], c_int),
+    "fpx_decode_attention_noalloc": ([P, *S3, P, *S3, P, *S3, c_int, c_int, c_int, c_int, c_int, c_int,
+                                      c_double, P, *S3, P, P], c_int),
     "fpx_prefill_export_routing": ([c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, c_size, P, P, P, P],
                                    c_int),
 }

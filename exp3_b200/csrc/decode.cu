@@ -7,6 +7,7 @@
 // once for the whole group), keeps an online softmax per head and writes a partial
 // (o, m, l) per split. Pass 2 merges the splits into bf16 O and a natural-log LSE.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -185,6 +186,86 @@ extern "C" int fpx_decode_attention(const void *q, int64_t q_sb, int64_t q_sl, i
   p.splits = (S + p.keys_per_split - 1) / p.keys_per_split;
   p.scale_log2 = (float)scale * kLog2e;
   p.part_o = static_cast<float *>(workspace);
+  p.part_ml = p.part_o + (size_t)B * Lq * H * p.splits * kHeadDim;
+  decode_split_kernel<<<dim3(p.splits, Hkv, B * Lq), 128, 0, stream>>>(p);
+  FPX_CHECK_LAUNCH();
+  decode_combine_kernel<<<dim3(H, B * Lq), 128, 0, stream>>>(p);
+  FPX_CHECK_LAUNCH();
+  return FPX_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Decode with no workspace argument and no allocation.
+//
+// Some callers cannot allocate device memory at the moment they decode: an inference engine
+// that only hands out memory from its own pre-sized pool, a plug-in invoked from inside another
+// runtime's step where calling the CUDA allocator is forbidden, or a C caller with no allocator
+// at all. For them this entry point keeps the split-K partials in one fixed array compiled into
+// the library (kDecodeScratchBytes per device, present on every GPU that loads the library
+// until the process exits) instead of a caller-provided workspace.
+//
+// The first call on a device looks up the array's device address with cudaGetSymbolAddress (the
+// array's name in host code is only a host-side stand-in, not a device address); make that
+// first call before any stream capture. Every call shares the one array and it keeps the last
+// call's contents: each call writes every partial it later reads, so nothing has to start at
+// zero, but calls that overlap on the GPU (different streams, no ordering) race on the array.
+namespace fpx {
+
+constexpr size_t kDecodeScratchBytes = FPX_DECODE_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_decode_scratch[kDecodeScratchBytes];
+
+static std::mutex g_decode_scratch_mutex;
+static void *g_decode_scratch_address[64];
+
+// Device address of g_decode_scratch on the current device (looked up once per device).
+static int decode_scratch_address(void **out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FPX_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return FPX_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(g_decode_scratch_mutex);
+  if (!g_decode_scratch_address[dev]) {
+    void *addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_decode_scratch) != cudaSuccess || !addr) return FPX_ERR_CUDA;
+    g_decode_scratch_address[dev] = addr;
+  }
+  *out = g_decode_scratch_address[dev];
+  return FPX_OK;
+}
+
+}  // namespace fpx
+
+extern "C" int fpx_decode_attention_noalloc(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                                            const void *k, int64_t k_sb, int64_t k_sl, int64_t k_sh,
+                                            const void *v, int64_t v_sb, int64_t v_sl, int64_t v_sh,
+                                            int B, int Lq, int S, int H, int Hkv, int d, double scale,
+                                            void *out, int64_t o_sb, int64_t o_sl, int64_t o_sh,
+                                            float *lse, fpx_stream_t stream) {
+  FPX_BIND(stream);
+  if (d != kHeadDim) return FPX_ERR_UNSUPPORTED;
+  if (!q || !k || !v || !out || B <= 0 || Lq <= 0 || S <= 0 || H <= 0 || Hkv <= 0)
+    return FPX_ERR_INVALID;
+  if (H % Hkv || H / Hkv > kMaxGroup || k_sl % 8 || k_sb % 8 || k_sh % 8 ||
+      (reinterpret_cast<uintptr_t>(k) & 15))
+    return FPX_ERR_SHAPE;
+  // Sizes whose partials do not fit the fixed array are refused before anything runs.
+  if (fpx_decode_workspace_bytes(B, Lq, H, Hkv, S, d) > kDecodeScratchBytes) return FPX_ERR_WORKSPACE;
+  void *scratch = nullptr;
+  const int rc = decode_scratch_address(&scratch);
+  if (rc != FPX_OK) return rc;
+  DecodeParams p{};
+  p.q = static_cast<const __nv_bfloat16 *>(q);
+  p.k = static_cast<const __nv_bfloat16 *>(k);
+  p.v = static_cast<const __nv_bfloat16 *>(v);
+  p.q_sb = q_sb; p.q_sl = q_sl; p.q_sh = q_sh;
+  p.k_sb = k_sb; p.k_sl = k_sl; p.k_sh = k_sh;
+  p.v_sb = v_sb; p.v_sl = v_sl; p.v_sh = v_sh;
+  p.out = static_cast<__nv_bfloat16 *>(out); p.o_sb = o_sb; p.o_sl = o_sl; p.o_sh = o_sh;
+  p.lse = lse; p.Lq = Lq; p.S = S; p.H = H; p.Hkv = Hkv; p.group = H / Hkv;
+  p.splits = decode_splits(B, Lq, Hkv, S);
+  p.keys_per_split = (((S + p.splits - 1) / p.splits) + kDecodeKeys - 1) / kDecodeKeys * kDecodeKeys;
+  p.splits = (S + p.keys_per_split - 1) / p.keys_per_split;
+  p.scale_log2 = (float)scale * kLog2e;
+  p.part_o = static_cast<float *>(scratch);
   p.part_ml = p.part_o + (size_t)B * Lq * H * p.splits * kHeadDim;
   decode_split_kernel<<<dim3(p.splits, Hkv, B * Lq), 128, 0, stream>>>(p);
   FPX_CHECK_LAUNCH();

@@ -197,6 +197,25 @@ int fpx_decode_attention(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh
                          void *out, int64_t o_sb, int64_t o_sl, int64_t o_sh, float *lse,
                          void *workspace, size_t workspace_bytes, fpx_stream_t stream);
 
+/* Decode that allocates nothing and takes no workspace. No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory where they decode (an engine that
+ * only hands out memory from its own fixed pool, a plug-in called inside another runtime's
+ * step, a C caller without an allocator). Same arguments and result as fpx_decode_attention
+ * minus the workspace; the split-K partials live in a fixed array of
+ * FPX_DECODE_NOALLOC_SCRATCH_BYTES compiled into the library, held on every GPU that loads
+ * it until the process exits. Problems whose partials
+ * (fpx_decode_workspace_bytes(B, Lq, H, Hkv, S, d)) exceed that size return
+ * FPX_ERR_WORKSPACE before anything runs. The first call on a device looks the array's
+ * address up (cudaGetSymbolAddress), so make it before any stream capture. All calls share
+ * the array: calls that overlap on the GPU race; nothing in it needs to start at zero. */
+#define FPX_DECODE_NOALLOC_SCRATCH_BYTES (2u << 20)
+int fpx_decode_attention_noalloc(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                                 const void *k, int64_t k_sb, int64_t k_sl, int64_t k_sh,
+                                 const void *v, int64_t v_sb, int64_t v_sl, int64_t v_sh,
+                                 int B, int Lq, int S, int H, int Hkv, int d, double scale,
+                                 void *out, int64_t o_sb, int64_t o_sl, int64_t o_sh, float *lse,
+                                 fpx_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
