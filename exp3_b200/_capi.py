@@ -126,6 +126,11 @@ def device_error(reset: bool = True) -> int:
 
 
 def set_exact_kernel(name: str) -> None:
-    """Selects the exact-attention kernel of the fused path: "tcgen05" (two query tiles per CTA,
-    the default), "tcgen05_single" (one tile per CTA) or "mma" (mma.sync cross-check)."""
-    call("fpx_set_option", 1, {"tcgen05": 0, "mma": 1, "tcgen05_single": 2}[name])
+    """Selects the exact-attention kernel of the fused path: "tcgen05" (the default) or "mma"
+    (the mma.sync cross-check)."""
+    call("fpx_set_option", 1, {"tcgen05": 0, "mma": 1}[name])
+
+
+def set_exp_emulation(pairs_of_8: int) -> None:
+    """How many of every 8 exp2 pairs the tcgen05 kernel evaluates on the FMA pipe (0, 2, 3)."""
+    call("fpx_set_option", 2, int(pairs_of_8))

@@ -1,23 +1,39 @@
 // Exact block-sparse causal attention on the 5th-generation tensor core (tcgen05 + TMEM + TMA).
 //
-// Reference semantics: upstream/flashprefill_native_forward.py:215-354 (_flash_forward) —
-// for query tile t (128 rows) of head h, attend over the tile's selected 128-key blocks in
-// ascending order with an online softmax in exp2 units, causal mask on the diagonal block,
-// P rounded to bf16 before P.V, bf16 output and natural-log LSE.
+// Reference semantics: upstream/flashprefill_native_forward.py:215-354 (_flash_forward) — for
+// query tile t (128 rows) of head h, attend over the tile's selected 128-key blocks in ascending
+// order with an online softmax in exp2 units, causal mask on the diagonal block, P rounded to
+// bf16 before P.V, bf16 output and natural-log LSE.
 //
-// One CTA per (batch, head, query tile), 192 threads in three roles:
-//   warp 0      TMA producer: Q once, then K and V of each selected block into a 2-stage ring;
-//   warp 1      MMA issuer (one elected lane): S = Q K^T into a double-buffered TMEM S, then
-//               O += P V into TMEM O once the softmax has published P;
-//   warps 2..5  softmax (thread = query row = TMEM lane): read S from TMEM, mask, online
-//               softmax, rescale O in TMEM when the row max grows, write P (bf16) into a
-//               swizzled shared tile, and finally normalise O and store it with TMA.
-// TMEM: columns [0,128) S0, [128,256) S1, [256,384) O (fp32, 128 lanes). Every mbarrier wait
-// is bounded; a wait that gives up flags the CTA, the roles drain and exit, and the host sees
-// FPX_ERR_TIMEOUT through fpx_device_error().
+// One CTA runs two query tiles: heads hA = kv*G + 2*pair and hB = hA + 1 of one KV group at the
+// same query tile t, so every K/V block loaded serves both (GQA sharing inside the CTA; no
+// cluster multicast). 384 threads in three warpgroups:
+//   warps 0..3   softmax of tile A       warps 4..7   softmax of tile B
+//   warp 8       TMA: Q, then the K ring warp 10      TMA: the V ring
+//   warp 9       MMA issuer (one elected lane)        warp 11 idle
+// The K and V rings stream the union of the two heads' block lists (each two stages, 128-byte
+// swizzle); a K stage is released as soon as the block's QK^T products are done, a V stage once
+// its P.V products are, so loads run well ahead of the tensor core. The MMA warp issues tile X's
+// products only for blocks in X's own list:
+//   S_X = Q_X K^T   (A = Q_X, B = K: both K-major in shared memory) into TMEM S_X,
+//   O_X += P_X V    (A = P_X read from TMEM, B = V MN-major in shared memory) into TMEM O_X.
+// TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512) fp32 columns x 128 lanes;
+// P_X (bf16, two per column) overwrites the first 64 columns of S_X once the softmax has read it.
+// While one tile runs its softmax the tensor core works on the other tile.
+//
+// Ordering facts the protocol relies on: a thread's tcgen05 MMAs complete in issue order and a
+// commit tracks all of the thread's earlier MMAs. So when s_full[X] fires for a block, the
+// previous P_X.V product has finished: O_X is stable and P_X's columns are free.
+//
+// Softmax (thread = query row = TMEM lane): the row max only moves when a block's max exceeds it
+// by more than 8 (log2 units), so P stays below 2^8 and O is rescaled rarely; O / l at the end is
+// exact either way. Scores are scaled with packed f32x2 FMAs; a fixed share of the exp2 pairs is
+// computed on the FMA pipe (exp2_poly2) to offload the special-function unit.
+//
+// Every mbarrier wait is bounded (about 1 s); a wait that gives up flags the CTA and the device
+// error word, the roles drain their in-flight copies and MMAs and exit, and later CTAs skip
+// their work, so a failed launch ends quickly and the host sees fpx_device_error() != 0.
 #include <cuda.h>
-
-#include <algorithm>
 
 #include "attn.cuh"
 #include "tc.cuh"
@@ -30,300 +46,24 @@ namespace {
 
 using namespace tc;
 
-constexpr int kStages = 2;
-constexpr int kThreads = 192;
-constexpr uint32_t kHalf = 128 * 128;  // 128 rows x 64 bf16 (one SW128 half tile)
+constexpr uint32_t kHalf = 128 * 128;  // 128 rows x 64 bf16: one SW128 half tile
 constexpr uint32_t kTile = 2 * kHalf;  // 128 x 128 bf16
 constexpr uint32_t kIdescQK = idesc_bf16(128, 128, false);
 constexpr uint32_t kIdescPV = idesc_bf16(128, 128, true);
-
-struct alignas(1024) Smem {
-  uint8_t q[kTile];
-  uint8_t k[kStages][kTile];
-  uint8_t v[kStages][kTile];
-  uint8_t p[kTile];
-  uint64_t q_full, k_full[kStages], v_full[kStages], kv_empty[kStages];
-  uint64_t s_full[2], s_empty[2], p_full, o_done, drain;
-  uint32_t tmem_base;
-  int abort;
-};
-
-// K-major SW128 operand (Q, K, P) at K offset 16*kk: halves of 64 columns sit kHalf apart,
-// 16 columns = 32 bytes inside a half.
-FPX_INLINE uint64_t desc_kmajor(const uint8_t *tile, int kk) {
-  const uint32_t a = smem_u32(tile) + (kk >> 2) * kHalf + (kk & 3) * 32;
-  return smem_desc_sw128(a, 16, 1024);
-}
-// MN-major SW128 V operand at key offset 16*kk: 16 keys = 16 rows of 128 bytes.
-FPX_INLINE uint64_t desc_v(const uint8_t *tile, int kk) {
-  return smem_desc_sw128(smem_u32(tile) + kk * 2048, kHalf, 1024);
-}
-
-// Byte offset of (row, col) inside a 128 x 128 bf16 SW128 K-major tile.
-FPX_INLINE uint32_t sw128_offset(int row, int col) {
-  const int half = col >> 6, chunk = (col & 63) >> 3;
-  return half * kHalf + row * 128 + ((chunk ^ (row & 7)) << 4) + ((col & 7) << 1);
-}
-
-}  // namespace
-
-__global__ void __launch_bounds__(kThreads, 1)
-    exact_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                    ExactParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  Smem &sh = *reinterpret_cast<Smem *>(smem_raw + pad);
-  volatile int *abort = &sh.abort;
-
-  const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);
-  const int h = p.head_begin + blockIdx.y;
-  const int b = blockIdx.z;
-  const int kvh = h / p.group;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t rrow = p.route.row(b, h, t, p.H);
-  // Once any CTA has given up on a wait, the rest skip their work (the launch is failed).
-  const int count = *reinterpret_cast<volatile int *>(&g_device_error) ? 0 : p.route.counts[rrow];
-  const int32_t *list = p.route.lists + rrow * p.route.nb;
-
-  if (threadIdx.x == 0) {
-    mbar_init(&sh.q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sh.k_full[s], 1);
-      mbar_init(&sh.v_full[s], 1);
-      mbar_init(&sh.kv_empty[s], 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&sh.s_full[s], 1);
-      mbar_init(&sh.s_empty[s], 128);
-    }
-    mbar_init(&sh.p_full, 128);
-    mbar_init(&sh.o_done, 1);
-    mbar_init(&sh.drain, 1);
-    sh.abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(&sh.tmem_base, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = sh.tmem_base;
-
-  if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
-    int issued[kStages] = {0, 0};
-    if (count > 0) {
-      if (lane == 0) {
-        mbar_expect_tx(&sh.q_full, kTile);
-        tma_load_4d(sh.q, &tm_q, &sh.q_full, 0, h, t * 128, b);
-        tma_load_4d(sh.q + kHalf, &tm_q, &sh.q_full, 64, h, t * 128, b);
-      }
-      for (int j = 0; j < count; ++j) {
-        const int s = j % kStages, n = j / kStages;
-        if (n > 0 && !mbar_wait_warp(&sh.kv_empty[s], (n - 1) & 1, abort)) break;
-        const int blk = list[j];
-        if (lane == 0) {
-          mbar_expect_tx(&sh.k_full[s], kTile);
-          tma_load_4d(sh.k[s], &tm_k, &sh.k_full[s], 0, kvh, blk * 128, b);
-          tma_load_4d(sh.k[s] + kHalf, &tm_k, &sh.k_full[s], 64, kvh, blk * 128, b);
-          mbar_expect_tx(&sh.v_full[s], kTile);
-          tma_load_4d(sh.v[s], &tm_v, &sh.v_full[s], 0, kvh, blk * 128, b);
-          tma_load_4d(sh.v[s] + kHalf, &tm_v, &sh.v_full[s], 64, kvh, blk * 128, b);
-        }
-        issued[s] = n + 1;
-      }
-      __syncwarp();
-      if (*abort) {  // drain copies still in flight before the CTA's shared memory goes away
-        int never = 0;
-        mbar_wait(&sh.q_full, 0, &never);
-        for (int s = 0; s < kStages; ++s)
-          if (issued[s] > 0) {
-            mbar_wait(&sh.k_full[s], (issued[s] - 1) & 1, &never);
-            mbar_wait(&sh.v_full[s], (issued[s] - 1) & 1, &never);
-          }
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (count > 0 && mbar_wait_warp(&sh.q_full, 0, abort)) {
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i % kStages;
-        if (!mbar_wait_warp(&sh.p_full, i & 1, abort)) return false;
-        if (!mbar_wait_warp(&sh.v_full[s], (i / kStages) & 1, abort)) return false;
-        tc_fence_after();
-        if (lane == 0) {
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ss(tmem + 256, desc_kmajor(sh.p, kk), desc_v(sh.v[s], kk), kIdescPV, (i > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(&sh.kv_empty[s]);
-          tc_commit(&sh.o_done);
-        }
-        __syncwarp();
-        return true;
-      };
-      bool ok = true;
-      for (int j = 0; j < count && ok; ++j) {
-        const int s = j % kStages, sb = j & 1;
-        if (!mbar_wait_warp(&sh.k_full[s], (j / kStages) & 1, abort)) break;
-        if (j >= 2 && !mbar_wait_warp(&sh.s_empty[sb], ((j >> 1) - 1) & 1, abort)) break;
-        tc_fence_after();
-        if (lane == 0) {
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ss(tmem + sb * 128, desc_kmajor(sh.q, kk), desc_kmajor(sh.k[s], kk), kIdescQK, kk > 0 ? 1u : 0u);
-          tc_commit(&sh.s_full[sb]);
-        }
-        __syncwarp();
-        if (j >= 1) ok = issue_pv(j - 1);
-      }
-      if (ok && !*abort) issue_pv(count - 1);
-      if (*abort) {  // let every MMA this thread issued finish before TMEM is released
-        int never = 0;
-        if (lane == 0) tc_commit(&sh.drain);
-        __syncwarp();
-        mbar_wait(&sh.drain, 0, &never);
-      }
-    }
-  } else {
-    // ---------------------------------------------------------------- softmax warpgroup
-    const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // query row in the tile == TMEM lane
-    const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
-    const int qrow = t * 128 + r;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < count && ok; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait_warp(&sh.s_full[sb], (j >> 1) & 1, abort)) { ok = false; break; }
-      tc_fence_after();
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + sb * 128 + 32 * c, *reinterpret_cast<float(*)[32]>(&s[32 * c]));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&sh.s_empty[sb]);
-      const int blk = list[j];
-      const int kmax = (blk == t) ? (r) : 127;  // diagonal block: key j <= row
-      float mx = m;
-#pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        const float x = (i <= kmax) ? s[i] * p.scale_log2 : -INFINITY;
-        s[i] = x;
-        mx = fmaxf(mx, x);
-      }
-      float rs = 0.f;
-      uint32_t pk[64];
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float a = (mx == -INFINITY) ? 0.f : exp2f(s[2 * i] - mx);
-        const float c = (mx == -INFINITY) ? 0.f : exp2f(s[2 * i + 1] - mx);
-        rs += a + c;
-        pk[i] = pack_bf16(a, c);
-      }
-      const float corr = (m == -INFINITY) ? (mx == -INFINITY ? 1.f : 0.f) : exp2f(m - mx);
-      if (j > 0) {
-        if (!mbar_wait_warp(&sh.o_done, (j - 1) & 1, abort)) { ok = false; break; }
-        if (__any_sync(0xffffffffu, corr != 1.f)) {  // tcgen05.ld/st are warp-collective
-          tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float o[32];
-            tmem_ld32(lane_addr + 256 + 32 * c, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= corr;
-            tmem_st32(lane_addr + 256 + 32 * c, o);
-          }
-          tmem_wait_st();
-        }
-      }
-      l = l * corr + rs;
-      m = mx;
-      // P row -> swizzled K-major tile (16-byte chunks).
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 v4 = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        *reinterpret_cast<uint4 *>(sh.p + sw128_offset(r, 8 * c)) = v4;
-      }
-      fence_proxy_async();
-      tc_fence_before();
-      mbar_arrive(&sh.p_full);
-    }
-    // Epilogue: O / l -> bf16 -> swizzled tile (in the Q buffer) -> TMA store; LSE.
-    if (ok && count > 0) {
-      if (!mbar_wait_warp(&sh.o_done, (count - 1) & 1, abort)) ok = false;
-    }
-    tc_fence_after();
-    const bool none = !(ok && count > 0) || m == -INFINITY;
-    const float inv = none ? 0.f : 1.f / l;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float o[32];
-      if (ok && count > 0) {
-        tmem_ld32(lane_addr + 256 + 32 * c, o);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint4 v4 = make_uint4(pack_bf16(o[8 * i] * inv, o[8 * i + 1] * inv), pack_bf16(o[8 * i + 2] * inv, o[8 * i + 3] * inv),
-                              pack_bf16(o[8 * i + 4] * inv, o[8 * i + 5] * inv), pack_bf16(o[8 * i + 6] * inv, o[8 * i + 7] * inv));
-        *reinterpret_cast<uint4 *>(sh.q + sw128_offset(r, 32 * c + 8 * i)) = v4;
-      }
-    }
-    if (p.lse && qrow < p.L) p.lse[((int64_t)b * p.L + qrow) * p.H + h] = none ? -INFINITY : m * kLn2 + logf(l);
-    fence_proxy_async();
-    named_sync(1, 128);
-    if (threadIdx.x == 64 && !*abort) {
-      tma_store_4d(&tm_o, sh.q, 0, h, t * 128, b);
-      tma_store_4d(&tm_o, sh.q + kHalf, 64, h, t * 128, b);
-      bulk_commit();
-      bulk_wait0();
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (threadIdx.x == 0 && sh.abort) atomicExch(&g_device_error, 1);
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// ============================================================================================
-// Two query tiles per CTA: heads hA = kv*G + 2*pair and hB = hA + 1 of one KV group, same
-// query tile t, so every K/V block loaded serves both. 320 threads:
-//   warps 0..3  softmax of tile A      warps 4..7  softmax of tile B
-//   warp 8      TMA producer           warp 9      MMA issuer
-// The producer streams the union of the two heads' block lists; the MMA warp issues tile X's
-// QK / PV only for blocks in X's own list. TMEM columns: S_A [0,128), S_B [128,256),
-// O_A [256,384), O_B [384,512); P_X (bf16, two per column) overwrites the first 64 columns of
-// S_X after the softmax has read S_X, and feeds P.V straight from TMEM. With both tiles in
-// flight the tensor core works on one tile while the other's softmax runs.
-//
-// Ordering facts the protocol relies on: the MMAs of one issuing thread complete in issue
-// order, and a commit tracks every earlier MMA of that thread. So when s_full[X] fires for
-// block i, PV_X(i-1) has finished: O_X is stable and P_X's columns are free.
-// The softmax keeps a running row max m and only moves it (rescaling O and l) when the block
-// max exceeds it by more than 8 (log2 units), so P stays below 2^8 and O is rarely touched;
-// O / l at the end is exact either way.
-namespace v2 {
-
-constexpr int kStages = 2;
-constexpr int kThreads = 320;
+constexpr int kKStages = 2, kVStages = 2;
+constexpr int kThreads = 384;
+// Launched at 168 registers per thread (384 x 168 = 64512). The control warpgroup gives
+// registers up so each softmax thread holds a full 128-column row of S without spilling:
+// 2 x 128 x 216 + 128 x 64 = 63488 <= 64512, and per SM sub-partition 216 + 216 + 64 <= 512.
+constexpr int kSoftmaxRegs = 216, kControlRegs = 64;
 constexpr int kMaxBlocks = 2048;  // union list capacity: L <= 262144
 constexpr float kRescaleThreshold = 8.f;
 
 struct alignas(1024) Smem {
   uint8_t q[2][kTile];  // Q of tiles A and B; reused to stage each tile's output
-  uint8_t k[kStages][kTile];
-  uint8_t v[kStages][kTile];
-  uint64_t q_full, k_full[kStages], v_full[kStages], kv_empty[kStages];
+  uint8_t k[kKStages][kTile];
+  uint8_t v[kVStages][kTile];
+  uint64_t q_full, k_full[kKStages], k_empty[kKStages], v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], p_full[2], o_done[2], drain;
   uint32_t tmem_base;
   int abort, n_union;
@@ -332,18 +72,69 @@ struct alignas(1024) Smem {
   uint8_t u_flags[kMaxBlocks];
 };
 
-}  // namespace v2
+// K-major SW128 operand (Q, K) at K offset 16*kk: halves of 64 columns sit kHalf apart,
+// 16 columns = 32 bytes inside a half; 8-row groups 1024 B apart.
+FPX_INLINE uint64_t desc_kmajor(const uint8_t *tile, int kk) {
+  return smem_desc_sw128(smem_u32(tile) + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+}
+// MN-major SW128 V operand at key offset 16*kk: 16 keys = 16 rows of 128 B; the two 64-column
+// halves (MN atoms) kHalf apart, 8-key groups 1024 B apart.
+FPX_INLINE uint64_t desc_v(const uint8_t *tile, int kk) {
+  return smem_desc_sw128(smem_u32(tile) + kk * 2048, kHalf, 1024);
+}
+// Byte offset of (row, col) inside a 128 x 128 bf16 SW128 K-major tile.
+FPX_INLINE uint32_t sw128_offset(int row, int col) {
+  const int half = col >> 6, chunk = (col & 63) >> 3;
+  return half * kHalf + row * 128 + ((chunk ^ (row & 7)) << 4) + ((col & 7) << 1);
+}
 
-__global__ void __launch_bounds__(v2::kThreads, 1)
-    exact_tc2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                     ExactParams p, int pairs) {
+// One 128-column row of P for a block: x = s * scale_log2 - m, p = 2^x, packed to bf16 into
+// TMEM (16 columns at a time); returns the row sum of p (fp32, before rounding, as the
+// reference's tile_denominator). kEmu of every 8 pairs use the FMA-pipe exp2.
+template <int kEmu>
+FPX_INLINE float softmax_row(const float (&sv)[128], float sl2, float neg, uint32_t p_addr) {
+  const uint64_t sl2x2 = pk2(sl2, sl2), negx2 = pk2(neg, neg);
+  uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int q4 = 0; q4 < 4; ++q4) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const uint64_t xx = ffma2(pk2(sv[32 * q4 + 2 * c], sv[32 * q4 + 2 * c + 1]), sl2x2, negx2);
+      uint64_t pp;
+      if ((c & 7) < kEmu) {
+        pp = exp2_poly2(xx);
+      } else {
+        float a, e;
+        up2(xx, a, e);
+        pp = pk2(ex2(a), ex2(e));
+      }
+      acc[c & 3] = fadd2(acc[c & 3], pp);
+      pk[c] = cvt_bf16x2(pp);
+    }
+    tmem_st16u(p_addr + 16 * q4, pk);
+  }
+  float a0, a1, a2, a3, b0, b1, b2, b3;
+  up2(acc[0], a0, b0);
+  up2(acc[1], a1, b1);
+  up2(acc[2], a2, b2);
+  up2(acc[3], a3, b3);
+  return ((a0 + b0) + (a1 + b1)) + ((a2 + b2) + (a3 + b3));
+}
+
+}  // namespace
+
+template <int kEmu>
+__global__ void __launch_bounds__(kThreads, 1)
+    exact_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                    ExactParams p, int pairs) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  v2::Smem &sh = *reinterpret_cast<v2::Smem *>(smem_raw + pad);
+  Smem &sh = *reinterpret_cast<Smem *>(smem_raw + pad);
   volatile int *abort = &sh.abort;
 
-  const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);
+  const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);  // longest tiles first
   const int pair = blockIdx.y % pairs;
   const int kvh = p.head_begin / p.group + blockIdx.y / pairs;
   const int b = blockIdx.z;
@@ -364,10 +155,13 @@ __global__ void __launch_bounds__(v2::kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sh.q_full, 1);
-    for (int s = 0; s < v2::kStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(&sh.k_full[s], 1);
+      mbar_init(&sh.k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(&sh.v_full[s], 1);
-      mbar_init(&sh.kv_empty[s], 1);
+      mbar_init(&sh.v_empty[s], 1);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&sh.s_full[x], 1);
@@ -378,14 +172,14 @@ __global__ void __launch_bounds__(v2::kThreads, 1)
     sh.abort = 0;
     fence_barrier_init();
   }
-  for (int w = threadIdx.x; w < 2 * (v2::kMaxBlocks / 32); w += v2::kThreads) (&sh.bits[0][0])[w] = 0u;
+  for (int w = threadIdx.x; w < 2 * (kMaxBlocks / 32); w += kThreads) (&sh.bits[0][0])[w] = 0u;
   if (warp == 9) {
     tmem_alloc(&sh.tmem_base, 512);
     tmem_relinquish();
   }
   __syncthreads();
   for (int x = 0; x < 2; ++x)
-    for (int i = threadIdx.x; i < cnt[x]; i += v2::kThreads) {
+    for (int i = threadIdx.x; i < cnt[x]; i += kThreads) {
       const int blk = lists[x][i];
       atomicOr(&sh.bits[x][blk >> 5], 1u << (blk & 31));
     }
@@ -404,8 +198,8 @@ __global__ void __launch_bounds__(v2::kThreads, 1)
         if (lane >= o) incl += y;
       }
       int pos = base + incl - n;
-      for (uint32_t x = u; x; x &= x - 1) {
-        const int bit = __ffs(x) - 1;
+      for (uint32_t bits = u; bits; bits &= bits - 1) {
+        const int bit = __ffs(bits) - 1;
         sh.u_blk[pos] = (uint16_t)(32 * w + bit);
         sh.u_flags[pos] = (uint8_t)(((a >> bit) & 1u) | (((c >> bit) & 1u) << 1));
         ++pos;
@@ -421,98 +215,109 @@ __global__ void __launch_bounds__(v2::kThreads, 1)
   const int n_union = sh.n_union;
   const int n_tiles = has_b ? 2 : 1;
 
-  if (warp == 8) {
-    // ---------------------------------------------------------------- TMA producer
-    int issued[v2::kStages] = {0, 0};
-    if (n_union > 0) {
-      if (lane == 0) {
-        mbar_expect_tx(&sh.q_full, kTile * n_tiles);
-        for (int x = 0; x < n_tiles; ++x) {
-          tma_load_4d(sh.q[x], &tm_q, &sh.q_full, 0, heads[x], t * 128, b);
-          tma_load_4d(sh.q[x] + kHalf, &tm_q, &sh.q_full, 64, heads[x], t * 128, b);
-        }
-      }
-      for (int u = 0; u < n_union; ++u) {
-        const int s = u % v2::kStages, n = u / v2::kStages;
-        if (n > 0 && !mbar_wait_warp(&sh.kv_empty[s], (n - 1) & 1, abort)) break;
-        const int blk = sh.u_blk[u];
-        if (lane == 0) {
-          mbar_expect_tx(&sh.k_full[s], kTile);
-          tma_load_4d(sh.k[s], &tm_k, &sh.k_full[s], 0, kvh, blk * 128, b);
-          tma_load_4d(sh.k[s] + kHalf, &tm_k, &sh.k_full[s], 64, kvh, blk * 128, b);
-          mbar_expect_tx(&sh.v_full[s], kTile);
-          tma_load_4d(sh.v[s], &tm_v, &sh.v_full[s], 0, kvh, blk * 128, b);
-          tma_load_4d(sh.v[s] + kHalf, &tm_v, &sh.v_full[s], 64, kvh, blk * 128, b);
-        }
-        issued[s] = n + 1;
-      }
-      __syncwarp();
-      if (*abort) {
-        int never = 0;
-        mbar_wait(&sh.q_full, 0, &never);
-        for (int s = 0; s < v2::kStages; ++s)
-          if (issued[s] > 0) {
-            mbar_wait(&sh.k_full[s], (issued[s] - 1) & 1, &never);
-            mbar_wait(&sh.v_full[s], (issued[s] - 1) & 1, &never);
+  if (warp >= 8) {
+    regs_dec<kControlRegs>();
+    if (warp == 8 || warp == 10) {
+      // ------------------------------------------------------------ TMA producers (K / V rings)
+      const bool is_k = warp == 8;
+      const int stages = is_k ? kKStages : kVStages;
+      uint64_t *full = is_k ? sh.k_full : sh.v_full;
+      uint64_t *empty = is_k ? sh.k_empty : sh.v_empty;
+      const CUtensorMap *map = is_k ? &tm_k : &tm_v;
+      int issued[2] = {0, 0};
+      if (n_union > 0) {
+        if (is_k && lane == 0) {
+          mbar_expect_tx(&sh.q_full, kTile * n_tiles);
+          for (int x = 0; x < n_tiles; ++x) {
+            tma_load_4d(sh.q[x], &tm_q, &sh.q_full, 0, heads[x], t * 128, b);
+            tma_load_4d(sh.q[x] + kHalf, &tm_q, &sh.q_full, 64, heads[x], t * 128, b);
           }
-      }
-    }
-  } else if (warp == 9) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (n_union > 0 && mbar_wait_warp(&sh.q_full, 0, abort)) {
-      int pend[2] = {-1, -1}, n_pv[2] = {0, 0};
-      // P.V of tile x for its pending block; releases the K/V stage once no tile needs it.
-      auto flush = [&](int x) -> bool {
-        const int u = pend[x], s = u % v2::kStages;
-        if (!mbar_wait_warp(&sh.p_full[x], n_pv[x] & 1, abort)) return false;
-        if (!mbar_wait_warp(&sh.v_full[s], (u / v2::kStages) & 1, abort)) return false;
-        tc_fence_after();
-        if (lane == 0) {
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ts(tmem + 256 + 128 * x, tmem + 128 * x + 8 * kk, desc_v(sh.v[s], kk), kIdescPV,
-                   (n_pv[x] > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(&sh.o_done[x]);
-          if (pend[x ^ 1] != u) tc_commit(&sh.kv_empty[s]);
+        }
+        for (int u = 0; u < n_union; ++u) {
+          const int s = u % stages, n = u / stages;
+          if (n > 0 && !mbar_wait_warp(&empty[s], (n - 1) & 1, abort)) break;
+          const int blk = sh.u_blk[u];
+          uint8_t *dst = is_k ? sh.k[s] : sh.v[s];
+          if (lane == 0) {
+            mbar_expect_tx(&full[s], kTile);
+            tma_load_4d(dst, map, &full[s], 0, kvh, blk * 128, b);
+            tma_load_4d(dst + kHalf, map, &full[s], 64, kvh, blk * 128, b);
+          }
+          issued[s] = n + 1;
         }
         __syncwarp();
-        ++n_pv[x];
-        pend[x] = -1;
-        return true;
-      };
-      bool ok = true;
-      for (int u = 0; u < n_union && ok; ++u) {
-        const int s = u % v2::kStages;
-        for (int x = 0; x < 2 && ok; ++x)
-          if (u >= v2::kStages && pend[x] == u - v2::kStages) ok = flush(x);
-        if (!ok || !mbar_wait_warp(&sh.k_full[s], (u / v2::kStages) & 1, abort)) break;
-        const int flags = sh.u_flags[u];
-        for (int x = 0; x < 2 && ok; ++x) {
-          if (!(flags & (1 << x))) continue;
-          if (pend[x] >= 0 && !(ok = flush(x))) break;
+        if (*abort) {  // drain copies still in flight before the shared memory goes away
+          int never = 0;
+          if (is_k) mbar_wait(&sh.q_full, 0, &never);
+          for (int s = 0; s < stages; ++s)
+            if (issued[s] > 0) mbar_wait(&full[s], (issued[s] - 1) & 1, &never);
+        }
+      }
+    } else if (warp == 9) {
+      // ------------------------------------------------------------ MMA issuer
+      if (n_union > 0 && mbar_wait_warp(&sh.q_full, 0, abort)) {
+        int pend[2] = {-1, -1}, n_pv[2] = {0, 0};
+        // P.V of tile x for its pending block; frees the V stage once no tile still needs it.
+        auto flush = [&](int x) -> bool {
+          const int u = pend[x], s = u % kVStages;
+          if (!mbar_wait_warp(&sh.p_full[x], n_pv[x] & 1, abort)) return false;
+          if (!mbar_wait_warp(&sh.v_full[s], (u / kVStages) & 1, abort)) return false;
           tc_fence_after();
           if (lane == 0) {
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
-              mma_ss(tmem + 128 * x, desc_kmajor(sh.q[x], kk), desc_kmajor(sh.k[s], kk), kIdescQK,
-                     kk > 0 ? 1u : 0u);
-            tc_commit(&sh.s_full[x]);
+              mma_ts(tmem + 256 + 128 * x, tmem + 128 * x + 8 * kk, desc_v(sh.v[s], kk), kIdescPV,
+                     (n_pv[x] > 0 || kk > 0) ? 1u : 0u);
+            tc_commit(&sh.o_done[x]);
+            if (pend[x ^ 1] != u) tc_commit(&sh.v_empty[s]);
           }
           __syncwarp();
-          pend[x] = u;
+          ++n_pv[x];
+          pend[x] = -1;
+          return true;
+        };
+        bool ok = true;
+        for (int u = 0; u < n_union && ok; ++u) {
+          const int s = u % kKStages;
+          // The V producer refills this block's V stage only after block u - kVStages's P.V.
+          for (int x = 0; x < 2 && ok; ++x)
+            if (u >= kVStages && pend[x] == u - kVStages) ok = flush(x);
+          const int flags = sh.u_flags[u];
+          bool have_k = false;
+          for (int x = 0; x < 2 && ok; ++x) {
+            if (!(flags & (1 << x))) continue;
+            if (pend[x] >= 0 && !(ok = flush(x))) break;
+            if (!have_k && !(ok = mbar_wait_warp(&sh.k_full[s], (u / kKStages) & 1, abort))) break;
+            have_k = true;
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk)
+                mma_ss(tmem + 128 * x, desc_kmajor(sh.q[x], kk), desc_kmajor(sh.k[s], kk), kIdescQK,
+                       kk > 0 ? 1u : 0u);
+              tc_commit(&sh.s_full[x]);
+            }
+            __syncwarp();
+            pend[x] = u;
+          }
+          if (ok && have_k) {  // both tiles' QK^T of block u issued: its K stage can be refilled
+            if (lane == 0) tc_commit(&sh.k_empty[s]);
+            __syncwarp();
+          }
         }
-      }
-      for (int x = 0; x < 2 && ok && !*abort; ++x)
-        if (pend[x] >= 0) ok = flush(x);
-      if (*abort) {
-        int never = 0;
-        if (lane == 0) tc_commit(&sh.drain);
-        __syncwarp();
-        mbar_wait(&sh.drain, 0, &never);
+        for (int x = 0; x < 2 && ok && !*abort; ++x)
+          if (pend[x] >= 0) ok = flush(x);
+        if (*abort) {  // let every MMA this thread issued finish before TMEM is released
+          int never = 0;
+          if (lane == 0) tc_commit(&sh.drain);
+          __syncwarp();
+          mbar_wait(&sh.drain, 0, &never);
+        }
       }
     }
   } else {
-    // ---------------------------------------------------------------- softmax, tile x
+    regs_inc<kSoftmaxRegs>();
+    // -------------------------------------------------------------- softmax of tile x
     const int x = warp >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
@@ -522,19 +327,24 @@ __global__ void __launch_bounds__(v2::kThreads, 1)
     const bool live = x == 0 || has_b;
     const int h = heads[x];
     const int n = cnt[x];
-    const int32_t *list = lists[x];
     const int qrow = t * 128 + r;
     const float sl2 = p.scale_log2;
+    // Lists are ascending and end at most at t, so only the last block can be the diagonal.
+    const bool last_is_diag = n > 0 && lists[x][n - 1] == t;
     float m = -INFINITY, l = 0.f;
     bool ok = live;
     for (int i = 0; i < n && ok; ++i) {
-      if (!mbar_wait_warp(&sh.s_full[x], i & 1, abort)) { ok = false; break; }
+      if (!mbar_wait_warp(&sh.s_full[x], i & 1, abort)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       float sv[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, *reinterpret_cast<float(*)[32]>(&sv[32 * c]));
       tmem_wait_ld();
-      if (list[i] == t) {  // diagonal block: key j visible to row r iff j <= r
+      const bool diag = last_is_diag && i == n - 1;
+      if (diag) {  // key j of the diagonal block is visible to row r iff j <= r
 #pragma unroll
         for (int c = 0; c < 128; ++c) sv[c] = c <= r ? sv[c] : -INFINITY;
       }
@@ -547,27 +357,15 @@ __global__ void __launch_bounds__(v2::kThreads, 1)
                                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
       const float mn = fmaxf(m, bmax);
       float corr = 1.f;
-      const bool move = __any_sync(0xffffffffu, mn > m + v2::kRescaleThreshold || m == -INFINITY);
+      const bool move = __any_sync(0xffffffffu, mn > m + kRescaleThreshold || m == -INFINITY);
       if (move) {
         corr = (m == -INFINITY) ? 0.f : ex2(m - mn);
         l *= corr;
         m = mn;
       }
       const float neg = (m == -INFINITY) ? 0.f : -m;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {  // 32 scores -> 16 packed columns of P at a time
-        uint32_t pk[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const float a = ex2(fmaf(sv[32 * q4 + 2 * c], sl2, neg));
-          const float e = ex2(fmaf(sv[32 * q4 + 2 * c + 1], sl2, neg));
-          acc[c & 3] += a + e;
-          pk[c] = pack_bf16(a, e);
-        }
-        tmem_st16u(s_addr + 16 * q4, pk);
-      }
-      l += (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      // The diagonal block's masked entries are -inf: the MUFU returns exactly 0 for them.
+      l += diag ? softmax_row<0>(sv, sl2, neg, s_addr) : softmax_row<kEmu>(sv, sl2, neg, s_addr);
       // O_X holds blocks < i and no P.V runs until p_full: rescale it for the moved max.
       if (move && i > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
@@ -585,6 +383,7 @@ __global__ void __launch_bounds__(v2::kThreads, 1)
       mbar_arrive(&sh.p_full[x]);
     }
     if (live) {
+      // Epilogue: O / l -> bf16 -> swizzled tile (in this tile's Q buffer) -> TMA store; LSE.
       if (ok && n > 0 && !mbar_wait_warp(&sh.o_done[x], (n - 1) & 1, abort)) ok = false;
       tc_fence_after();
       const bool none = !(ok && n > 0) || m == -INFINITY;
@@ -601,10 +400,10 @@ __global__ void __launch_bounds__(v2::kThreads, 1)
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          uint4 v4 = make_uint4(pack_bf16(o[8 * e] * inv, o[8 * e + 1] * inv),
-                                pack_bf16(o[8 * e + 2] * inv, o[8 * e + 3] * inv),
-                                pack_bf16(o[8 * e + 4] * inv, o[8 * e + 5] * inv),
-                                pack_bf16(o[8 * e + 6] * inv, o[8 * e + 7] * inv));
+          const uint4 v4 = make_uint4(pack_bf16(o[8 * e] * inv, o[8 * e + 1] * inv),
+                                      pack_bf16(o[8 * e + 2] * inv, o[8 * e + 3] * inv),
+                                      pack_bf16(o[8 * e + 4] * inv, o[8 * e + 5] * inv),
+                                      pack_bf16(o[8 * e + 6] * inv, o[8 * e + 7] * inv));
           *reinterpret_cast<uint4 *>(sh.q[x] + sw128_offset(r, 32 * c + 8 * e)) = v4;
         }
       }
@@ -647,8 +446,9 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int64_t rows, int64_t batch, int64_t sh,
-               int64_t sl, int64_t sb) {
+// [B, rows, heads, 128] bf16 with element strides -> 4-D map (d, head, row, batch), box 64 x 1 x 128 x 1.
+bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int64_t rows, int64_t batch,
+               int64_t sh, int64_t sl, int64_t sb) {
   cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)batch};
   cuuint64_t strides[3] = {(cuuint64_t)(sh * 2), (cuuint64_t)(sl * 2), (cuuint64_t)(sb * 2)};
   cuuint32_t box[4] = {64, 1, 128, 1};
@@ -658,35 +458,38 @@ bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int
   if (batch == 1) strides[2] = strides[1] * (cuuint64_t)rows;
   const EncodeTiledFn encode = encode_fn();
   if (!encode) return false;
-  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides,
-                                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int kEmu>
+void launch_variant(dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap &tq, const CUtensorMap &tk,
+                    const CUtensorMap &tv, const CUtensorMap &to, const ExactParams &p, int pairs) {
+  cudaFuncSetAttribute(exact_tc_kernel<kEmu>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  exact_tc_kernel<kEmu><<<grid, kThreads, smem, s>>>(tq, tk, tv, to, p, pairs);
 }
 
 }  // namespace
 
 size_t exact_tc_smem() { return sizeof(Smem) + 1024; }
-size_t exact_tc2_smem() { return sizeof(v2::Smem) + 1024; }
 
 int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s) {
   if (tiles <= 0 || heads <= 0) return FPX_OK;
+  if (p.route.nb > kMaxBlocks) return FPX_ERR_UNSUPPORTED;
   CUtensorMap tq, tk, tv, to;
   if (!encode_4d(&tq, p.q, kHeadDim, p.H, L, B, p.q_sh, p.q_sl, p.q_sb) ||
       !encode_4d(&tk, p.k, kHeadDim, Hkv, L, B, p.k_sh, p.k_sl, p.k_sb) ||
       !encode_4d(&tv, p.v, kHeadDim, Hkv, L, B, p.v_sh, p.v_sl, p.v_sb) ||
       !encode_4d(&to, p.out, kHeadDim, p.H, L, B, p.o_sh, p.o_sl, p.o_sb))
     return FPX_ERR_INVALID;
-  if (get_option(kOptExactKernel) == kExactKernelTcgen05Single) {
-    const size_t smem = exact_tc_smem();
-    cudaFuncSetAttribute(exact_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    exact_tc_kernel<<<dim3(tiles, heads, B), kThreads, smem, s>>>(tq, tk, tv, to, p);
-  } else {
-    if (p.route.nb > v2::kMaxBlocks) return FPX_ERR_UNSUPPORTED;
-    const int pairs = (p.group + 1) / 2;
-    const size_t smem = exact_tc2_smem();
-    cudaFuncSetAttribute(exact_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    exact_tc2_kernel<<<dim3(tiles, (heads / p.group) * pairs, B), v2::kThreads, smem, s>>>(tq, tk, tv, to, p,
-                                                                                            pairs);
+  const int pairs = (p.group + 1) / 2;
+  const dim3 grid(tiles, (heads / p.group) * pairs, B);
+  const size_t smem = exact_tc_smem();
+  switch (get_option(kOptExpEmulation)) {
+    case 0: launch_variant<0>(grid, smem, s, tq, tk, tv, to, p, pairs); break;
+    case 3: launch_variant<3>(grid, smem, s, tq, tk, tv, to, p, pairs); break;
+    default: launch_variant<2>(grid, smem, s, tq, tk, tv, to, p, pairs); break;
   }
   FPX_CHECK_LAUNCH();
   return FPX_OK;

@@ -77,7 +77,8 @@ int get_option(int key) { return (key > 0 && key < 4) ? g_options[key] : 0; }
 }  // namespace fpx
 
 extern "C" int fpx_set_option(int key, int value) {
-  if (key == kOptExactKernel && value >= kExactKernelTcgen05 && value <= kExactKernelTcgen05Single) {
+  if ((key == kOptExactKernel && (value == kExactKernelTcgen05 || value == kExactKernelMmaSync)) ||
+      (key == kOptExpEmulation && (value == 0 || value == 2 || value == 3))) {
     g_options[key] = value;
     return FPX_OK;
   }

@@ -81,6 +81,12 @@ FPX_INLINE void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "m
 // Named barrier among `count` threads.
 FPX_INLINE void named_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
 
+// Register reallocation between warpgroups (all four warps of a warpgroup execute it).
+template <int N>
+FPX_INLINE void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+FPX_INLINE void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+
 // ---- tcgen05 / TMEM ----------------------------------------------------------------------
 FPX_INLINE void tmem_alloc(uint32_t *dst_smem, uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
@@ -119,6 +125,50 @@ FPX_INLINE float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes of work).
+FPX_INLINE uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+FPX_INLINE void up2(uint64_t v, float &a, float &b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+FPX_INLINE uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+FPX_INLINE uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// 2^x for a pair on the FMA pipe, to offload the special-function unit. Range reduction
+// x = j + f with j = round(x) (the 1.5 * 2^23 magic-number add) and |f| <= 1/2, a cubic
+// for 2^f fitted here by a relative-error weighted least-squares fit on Chebyshev nodes
+// (max relative error 7.5e-5, 26x below bf16's rounding step), and 2^j added into the
+// exponent bits. x is clamped to >= -126 so the exponent never underflows.
+FPX_INLINE uint64_t exp2_poly2(uint64_t x2) {
+  float a, b;
+  up2(x2, a, b);
+  x2 = pk2(fmaxf(a, -126.f), fmaxf(b, -126.f));
+  const uint64_t magic = pk2(12582912.f, 12582912.f), nmagic = pk2(-12582912.f, -12582912.f);
+  const uint64_t minus1 = pk2(-1.f, -1.f);
+  const uint64_t t = fadd2(x2, magic);
+  const uint64_t f = ffma2(fadd2(t, nmagic), minus1, x2);
+  uint64_t poly = ffma2(f, pk2(0.05517113208770752f, 0.05517113208770752f), pk2(0.2426110804080963f, 0.2426110804080963f));
+  poly = ffma2(poly, f, pk2(0.6932610869407654f, 0.6932610869407654f));
+  poly = ffma2(poly, f, pk2(0.9999280571937561f, 0.9999280571937561f));
+  float pa, pb, ta, tb;
+  up2(poly, pa, pb);
+  up2(t, ta, tb);
+  return pk2(__uint_as_float(__float_as_uint(pa) + (__float_as_uint(ta) << 23)),
+             __uint_as_float(__float_as_uint(pb) + (__float_as_uint(tb) << 23)));
+}
+FPX_INLINE uint32_t cvt_bf16x2(uint64_t v) {
+  float a, b;
+  up2(v, a, b);
+  return pack_bf16(a, b);
 }
 FPX_INLINE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 FPX_INLINE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }

@@ -26,13 +26,15 @@ def main():
     ap.add_argument("--alpha", type=float, default=0.08)
     ap.add_argument("--repeats", type=int, default=3)
     ap.add_argument("--variant", default="iid", choices=["iid", "structured"])
-    ap.add_argument("--kernel", default="tcgen05", choices=["tcgen05", "tcgen05_single", "mma"])
+    ap.add_argument("--kernel", default="tcgen05", choices=["tcgen05", "mma"])
+    ap.add_argument("--emulate", type=int, default=0, choices=[0, 2, 3])
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     shape = synthetic.LayerShape(1, args.length, args.heads, args.kv_heads)
     q, k, v = synthetic.attention_inputs(shape, seed=0, needles=32, device=dev,
                                          structured_sigma=0.5 if args.variant == "structured" else 0.0)
     _capi.set_exact_kernel(args.kernel)
+    _capi.set_exp_emulation(args.emulate)
     out = torch.empty_like(q)
     scale = 128 ** -0.5
     times = {}

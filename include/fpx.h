@@ -64,9 +64,10 @@ enum fpx_stage {
 const char *fpx_status_string(int status);
 int fpx_version(void);
 
-/* Process-wide options (no reference counterpart): key 1 selects the exact-attention kernel
- * of fpx_prefill_attention — 0 = tcgen05/TMEM/TMA with two query tiles per CTA (default),
- * 1 = mma.sync (cross-check), 2 = tcgen05 with one query tile per CTA. */
+/* Process-wide options (no reference counterpart). Key 1 selects the exact-attention kernel of
+ * fpx_prefill_attention: 0 = tcgen05/TMEM/TMA, two query tiles per CTA (default), 1 = mma.sync
+ * (cross-check). Key 2 sets how many of every 8 exp2 pairs the tcgen05 kernel evaluates with
+ * an FMA-pipe polynomial instead of the special-function unit: 0 (default), 2 or 3. */
 int fpx_set_option(int key, int value);
 
 /* Reads (and with reset != 0 clears) the device error word set when a bounded wait inside a
