@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--alpha", type=float, default=0.08)
     ap.add_argument("--variant", default="iid", choices=["iid", "structured"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="layer", choices=["layer", "model"],
+                    help="layer: the 32K attention layer (default); model: full-model prefill + decode")
+    ap.add_argument("--prompt-length", type=int, default=32640)
+    ap.add_argument("--decode-tokens", type=int, default=128)
     return ap.parse_args()
 
 
@@ -188,6 +192,83 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_model(args, rank, world, local):
+    """Config 3: random-init Qwen2.5-7B, 32640-token prompt (uniform ids + 64 planted 16-token
+    key -> value spans), sparse prefill then 128 dense greedy decode tokens; tensor parallel on N GPUs."""
+    import datetime
+
+    import torch.distributed as dist
+    from exp3_b200.model import QWEN25_7B, AttentionSettings, Qwen2Model, synthetic_prompt
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    model = Qwen2Model(QWEN25_7B, device=dev, seed=0, tp_rank=rank, tp_size=world,
+                       attention=AttentionSettings(args.method, args.alpha))
+    ids_host = synthetic_prompt(args.prompt_length, QWEN25_7B.vocab_size).pin_memory()
+    ids = ids_host.to(dev)
+    for _ in range(args.warmup):
+        model.prefill(ids, args.decode_tokens)
+    torch.cuda.synchronize()
+
+    def timed(fn, n):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / n
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t)
+        return ms
+
+    with ClockSampler(local) as clocks:
+        prefill_ms = timed(lambda: model.prefill(ids, args.decode_tokens), args.steps)
+    first = model.prefill(ids, args.decode_tokens)
+
+    def decode_all():
+        model.length = args.prompt_length
+        tok = first
+        for _ in range(args.decode_tokens - 1):
+            tok = model.decode_step(tok)
+
+    decode_ms = timed(decode_all, 1) / max(1, args.decode_tokens - 1)
+    # End to end (evaluate.prefill): token ids from pinned host memory, prefill, first token to host.
+    result = torch.empty(1, dtype=torch.int64).pin_memory()
+
+    def e2e():
+        ids.copy_(ids_host, non_blocking=True)
+        result.copy_(model.prefill(ids, args.decode_tokens).view(1), non_blocking=True)
+
+    e2e_ms = timed(e2e, args.steps)
+    flops = model.prefill_flops(args.prompt_length)  # linear + all causal attention pairs
+    if rank == 0:
+        line = {"metric": "full-model prefill latency, Qwen2.5-7B shape, 32640 tokens", "value": prefill_ms,
+                "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": prefill_ms,
+                "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (random-init weights, seeded prompt)",
+                "config": {"workload": "config 3: random-init Qwen2.5-7B (28 layers, hidden 3584, 28/4 heads, "
+                                       "FFN 18944, vocab 152064), prompt 32640 ids with 64 planted 16-token spans",
+                           "method": args.method, "alpha": args.alpha,
+                           "parallelism": f"tp{world} (heads / FFN sharded, NCCL all-reduce after o_proj and down)",
+                           "prefill_tflops_dense_equivalent": flops / (prefill_ms * 1e-3) / 1e12,
+                           "decode_ms_per_token": decode_ms, "decode_tokens": args.decode_tokens},
+                "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": ids_host.numel() * 8,
+                        "d2h_bytes_per_step": 8},
+                "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -197,6 +278,8 @@ def main():
         raise SystemExit("at least 3 warm-up steps")
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.workload == "model":
+        return run_model(args, rank, world, local)
 
     import torch.distributed as dist
     from exp3_b200 import ops

@@ -1,0 +1,280 @@
+"""Qwen2.5-7B-shaped full-model prefill and greedy decode on libfpx, one GPU or tensor-parallel.
+
+The model exp3 times is HF ``Qwen2ForCausalLM`` driven by ``evaluate.prefill``
+(``evaluate.py:323-345``: one forward with ``logits_to_keep=1`` then argmax) and
+``evaluate.generate`` (``evaluate.py:357-405``: dense greedy decode on the KV cache), with
+the sparse prefill attention plugged in (``attention.py:57``). This module runs the same
+computation without the HF module graph:
+
+- the projections are plain cuBLAS GEMMs (through torch);
+- residual add + RMSNorm, RoPE and SwiGLU are libfpx kernels that keep HF's bf16 rounding
+  points;
+- attention is the fused libfpx prefill op on zero-copy views of the QKV output, and libfpx's
+  split-K decode kernel on the KV cache.
+
+Weights are random (seeded, normal(0, 0.02) like HF's initializer) because no checkpoint is
+available.
+
+Tensor parallelism (``tp_size`` > 1, one process per GPU, NCCL):
+- ranks own whole KV groups, or for ``tp_size`` > Hkv an equal split of one group's query
+  heads (Qwen2.5-7B on 8 GPUs: each KV head on two ranks with 4 + 3 query heads);
+- QKV and gate/up are column-sharded, o_proj and down_proj row-sharded;
+- o_proj and down_proj are each followed by an all-reduce.
+
+The embedding and LM head are replicated; only the last token's logits are computed.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import decode as _decode
+from . import ops
+from ._capi import FpxError, call, ptr, stream, strides3
+
+
+@dataclass(frozen=True)
+class Qwen2Config:
+    vocab_size: int = 152064
+    hidden_size: int = 3584
+    intermediate_size: int = 18944
+    num_hidden_layers: int = 28
+    num_attention_heads: int = 28
+    num_key_value_heads: int = 4
+    head_dim: int = 128
+    rope_theta: float = 1e6
+    rms_norm_eps: float = 1e-6
+    initializer_range: float = 0.02
+
+
+QWEN25_7B = Qwen2Config()
+
+
+def head_partition(cfg: Qwen2Config, rank: int, world: int):
+    """(kv heads, query heads) owned by ``rank``: whole KV groups, or a split of one group."""
+    hkv, heads = cfg.num_key_value_heads, cfg.num_attention_heads
+    group = heads // hkv
+    if world <= hkv:
+        if hkv % world:
+            raise ValueError(f"{hkv} KV heads do not split over {world} ranks")
+        per = hkv // world
+        kv = list(range(rank * per, (rank + 1) * per))
+        return kv, [h for k in kv for h in range(k * group, (k + 1) * group)]
+    if world % hkv:
+        raise ValueError(f"{world} ranks do not split {hkv} KV heads evenly")
+    parts = world // hkv
+    kv = rank // parts
+    j = rank % parts
+    size = [group // parts + (1 if i < group % parts else 0) for i in range(parts)]
+    start = kv * group + sum(size[:j])
+    return [kv], list(range(start, start + size[j]))
+
+
+def ffn_partition(cfg: Qwen2Config, rank: int, world: int):
+    per = cfg.intermediate_size // world
+    if cfg.intermediate_size % world:
+        raise ValueError("intermediate size does not split evenly")
+    return rank * per, (rank + 1) * per
+
+
+class _Init:
+    """Seeded normal(0, std) tensors, identical on every rank (each generates, then slices)."""
+
+    def __init__(self, seed: int, device):
+        self.gen = torch.Generator(device=device)
+        self.gen.manual_seed(seed)
+        self.device = device
+
+    def normal(self, shape, std):
+        return (torch.randn(shape, generator=self.gen, device=self.device, dtype=torch.float32) * std).to(
+            torch.bfloat16)
+
+
+class LayerWeights:
+    def __init__(self, cfg: Qwen2Config, layer: int, seed: int, device, kv, qh, ffn):
+        d, hid = cfg.head_dim, cfg.hidden_size
+        init = _Init(seed * 1000 + layer, device)
+        std = cfg.initializer_range
+        wq = init.normal((cfg.num_attention_heads * d, hid), std)
+        wk = init.normal((cfg.num_key_value_heads * d, hid), std)
+        wv = init.normal((cfg.num_key_value_heads * d, hid), std)
+        bq = init.normal((cfg.num_attention_heads * d,), std)
+        bk = init.normal((cfg.num_key_value_heads * d,), std)
+        bv = init.normal((cfg.num_key_value_heads * d,), std)
+        wo = init.normal((hid, cfg.num_attention_heads * d), std)
+        wg = init.normal((cfg.intermediate_size, hid), std)
+        wu = init.normal((cfg.intermediate_size, hid), std)
+        wd = init.normal((hid, cfg.intermediate_size), std)
+        rows = lambda heads: torch.cat([torch.arange(h * d, (h + 1) * d, device=device) for h in heads])
+        qr, kr = rows(qh), rows(kv)
+        self.w_qkv = torch.cat([wq[qr], wk[kr], wv[kr]]).contiguous()
+        self.b_qkv = torch.cat([bq[qr], bk[kr], bv[kr]]).contiguous()
+        self.w_o = wo[:, qr].contiguous()
+        f0, f1 = ffn
+        self.w_gu = torch.cat([wg[f0:f1], wu[f0:f1]]).contiguous()
+        self.w_down = wd[:, f0:f1].contiguous()
+        self.ln1 = torch.ones(hid, dtype=torch.bfloat16, device=device)
+        self.ln2 = torch.ones(hid, dtype=torch.bfloat16, device=device)
+        # full tensors kept only for tests that rebuild an HF model from the same weights
+        self.full = dict(wq=wq, wk=wk, wv=wv, bq=bq, bk=bk, bv=bv, wo=wo, wg=wg, wu=wu, wd=wd)
+
+
+@dataclass
+class AttentionSettings:
+    method: str = "mean_native"
+    alpha: float = 0.08
+    sink: int = 2
+    window: int = 4
+    last_full: int = 2
+
+
+class Qwen2Model:
+    def __init__(self, cfg: Qwen2Config = QWEN25_7B, device=None, seed: int = 0, tp_rank: int = 0,
+                 tp_size: int = 1, group=None, attention: AttentionSettings | None = None, keep_full=False):
+        self.cfg = cfg
+        self.device = torch.device(device or "cuda")
+        self.tp_rank, self.tp_size, self.group = tp_rank, tp_size, group
+        self.attn = attention or AttentionSettings()
+        self.kv, self.qh = head_partition(cfg, tp_rank, tp_size)
+        self.ffn = ffn_partition(cfg, tp_rank, tp_size)
+        init = _Init(seed, self.device)
+        self.embed = init.normal((cfg.vocab_size, cfg.hidden_size), cfg.initializer_range)
+        self.layers = []
+        for i in range(cfg.num_hidden_layers):
+            lw = LayerWeights(cfg, i, seed, self.device, self.kv, self.qh, self.ffn)
+            if not keep_full:
+                lw.full = None
+            self.layers.append(lw)
+        self.norm = torch.ones(cfg.hidden_size, dtype=torch.bfloat16, device=self.device)
+        self.lm_head = _Init(seed + 7, self.device).normal((cfg.vocab_size, cfg.hidden_size), cfg.initializer_range)
+        self.scale = cfg.head_dim ** -0.5
+        self.k_cache = self.v_cache = None
+        self.length = 0
+
+    # ---------------------------------------------------------------- pieces
+    def _rmsnorm(self, x, weight, residual=None):
+        rows, hid = x.shape
+        out = torch.empty_like(x)
+        call("fpx_rmsnorm", ptr(x), ptr(residual), ptr(weight), self.cfg.rms_norm_eps, rows, hid, ptr(out),
+             ptr(residual), stream(self.device))
+        return out
+
+    def _rope(self, t, pos0):
+        call("fpx_rope_neox", ptr(t), *strides3(t), t.shape[0], t.shape[1], t.shape[2], t.shape[3], pos0,
+             self.cfg.rope_theta, stream(self.device))
+
+    def _silu_mul(self, gu):
+        rows, two_i = gu.shape
+        out = torch.empty(rows, two_i // 2, dtype=gu.dtype, device=gu.device)
+        call("fpx_silu_mul", ptr(gu), rows, two_i // 2, ptr(out), stream(self.device))
+        return out
+
+    def _all_reduce(self, t):
+        if self.tp_size > 1:
+            torch.distributed.all_reduce(t, group=self.group)
+        return t
+
+    def _alloc_cache(self, capacity):
+        shape = (self.cfg.num_hidden_layers, 1, capacity, len(self.kv), self.cfg.head_dim)
+        self.k_cache = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
+        self.v_cache = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
+
+    def _layer(self, i, h, x, pos0, length, decoding):
+        """One decoder layer: x = normed input rows; returns (h, partial down output)."""
+        cfg, lw = self.cfg, self.layers[i]
+        d = cfg.head_dim
+        hq, hkv = len(self.qh), len(self.kv)
+        qkv = torch.addmm(lw.b_qkv, x, lw.w_qkv.t())
+        q = qkv[:, : hq * d].view(1, length, hq, d)
+        k = qkv[:, hq * d:(hq + hkv) * d].view(1, length, hkv, d)
+        v = qkv[:, (hq + hkv) * d:].view(1, length, hkv, d)
+        self._rope(q, pos0)
+        self._rope(k, pos0)
+        self.k_cache[i, :, pos0:pos0 + length] = k
+        self.v_cache[i, :, pos0:pos0 + length] = v
+        if decoding:
+            kc, vc = self.k_cache[i, :, :pos0 + length], self.v_cache[i, :, :pos0 + length]
+            attn = _decode.decode_attention(q, kc, vc, self.scale)
+        else:
+            a = self.attn
+            attn = ops.prefill_attention(q, k, v, a.method, a.alpha, self.scale, a.sink, a.window, a.last_full)
+        o = self._all_reduce(attn.view(length, hq * d) @ lw.w_o.t())
+        x2 = self._rmsnorm(o, lw.ln2, residual=h)  # h += o
+        gu = x2 @ lw.w_gu.t()
+        down = self._all_reduce(self._silu_mul(gu) @ lw.w_down.t())
+        return h, down
+
+    def _forward(self, ids, pos0, decoding):
+        length = ids.shape[0]
+        h = torch.nn.functional.embedding(ids, self.embed)
+        x = self._rmsnorm(h, self.layers[0].ln1)
+        down = None
+        for i in range(self.cfg.num_hidden_layers):
+            if i > 0:
+                x = self._rmsnorm(down, self.layers[i].ln1, residual=h)  # h += down
+            h, down = self._layer(i, h, x, pos0, length, decoding)
+        last = self._rmsnorm(down[-1:].contiguous(), self.norm, residual=h[-1:].contiguous())
+        logits = (last @ self.lm_head.t()).float()  # bf16 LM head, as HF's lm_head
+        return logits[-1]
+
+    # ---------------------------------------------------------------- public
+    @torch.inference_mode()
+    def prefill(self, input_ids: torch.Tensor, max_new_tokens: int = 0):
+        """``evaluate.prefill``: one forward over the prompt; returns the first generated token (device)."""
+        if input_ids.dim() != 1:
+            raise ValueError("input_ids must be 1-D (batch 1, as exp3)")
+        length = input_ids.shape[0]
+        if self.k_cache is None or self.k_cache.shape[2] < length + max_new_tokens:
+            self._alloc_cache(length + max_new_tokens)
+        logits = self._forward(input_ids, 0, decoding=False)
+        self.length = length
+        return logits.argmax()
+
+    @torch.inference_mode()
+    def decode_step(self, token: torch.Tensor):
+        """One dense greedy decode step (``evaluate.py:384-400``); returns the next token (device)."""
+        logits = self._forward(token.view(1), self.length, decoding=True)
+        self.length += 1
+        return logits.argmax()
+
+    @torch.inference_mode()
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int):
+        token = self.prefill(input_ids, max_new_tokens)
+        out = [token]
+        for _ in range(max_new_tokens - 1):
+            token = self.decode_step(token)
+            out.append(token)
+        return torch.stack(out)
+
+    def prefill_flops(self, length: int, exact_pairs: int | None = None) -> float:
+        """Algorithmic FLOPs of one prefill: 2 x params x L for the linear layers (last-token LM
+        head) plus 4 d x exact pairs per layer (all causal pairs when ``exact_pairs`` is None)."""
+        cfg = self.cfg
+        d, hid = cfg.head_dim, cfg.hidden_size
+        per_layer = hid * (cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * d + \
+            cfg.num_attention_heads * d * hid + 3 * hid * cfg.intermediate_size
+        linear = 2 * per_layer * cfg.num_hidden_layers * length + 2 * hid * cfg.vocab_size
+        pairs = exact_pairs if exact_pairs is not None else \
+            cfg.num_attention_heads * length * (length + 1) // 2
+        return linear + 4 * d * pairs * cfg.num_hidden_layers
+
+
+def synthetic_prompt(length: int = 32640, vocab: int = 152064, spans: int = 64, span_len: int = 16,
+                     seed: int = 0) -> torch.Tensor:
+    """Uniform random token ids with ``spans`` planted repeated key -> value spans of
+    ``span_len`` tokens (each span appears twice, its copy later in the prompt)."""
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, vocab, (length,), generator=g)
+    half = length // 2
+    for _ in range(spans):
+        src = int(torch.randint(0, half - span_len, (1,), generator=g))
+        dst = int(torch.randint(half, length - span_len, (1,), generator=g))
+        ids[dst:dst + span_len] = ids[src:src + span_len]
+    return ids
+
+
+__all__ = ["Qwen2Config", "QWEN25_7B", "Qwen2Model", "AttentionSettings", "head_partition", "ffn_partition",
+           "synthetic_prompt", "FpxError", "math"]

@@ -181,6 +181,22 @@ int fpx_prefill_export_routing(int method, int B, int L, int H, int Hkv, int d, 
                                uint8_t *selected, int64_t *indices, int32_t *counts,
                                fpx_stream_t stream);
 
+/* ---- the Qwen2 decoder layer around attention (the model exp3 drives) ------------------ */
+
+/* Residual add + RMSNorm over rows of `hidden` bf16 (HF Qwen2RMSNorm rounding): with residual
+ * non-NULL, s = residual + x (bf16) is written to residual_out (may alias residual) and
+ * normalised; out = weight * bf16(s * rsqrt(mean(s^2) + eps)). */
+int fpx_rmsnorm(const void *x, const void *residual, const void *weight, double eps, int64_t rows, int hidden,
+                void *out, void *residual_out, fpx_stream_t stream);
+
+/* NeoX rotary embedding in place on a strided [B, L, heads, 128] bf16 view, positions
+ * pos0 .. pos0 + L - 1, inv_freq = theta^(-2i/128) (HF apply_rotary_pos_emb rounding). */
+int fpx_rope_neox(void *x, int64_t x_sb, int64_t x_sl, int64_t x_sh, int B, int L, int heads, int d, int pos0,
+                  double theta, fpx_stream_t stream);
+
+/* SwiGLU: out[r, j] = silu(gate_up[r, j]) * gate_up[r, inter + j] (bf16, HF Qwen2MLP rounding). */
+int fpx_silu_mul(const void *gate_up, int64_t rows, int inter, void *out, fpx_stream_t stream);
+
 /* ---- dense decode (attention.py:178-189) --------------------------------------------- */
 
 /* Device bytes of workspace fpx_decode_attention needs. */
