@@ -30,6 +30,8 @@ import torch
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+# Keep rank 0's stdout to the one JSON line (NCCL otherwise announces its version there).
+os.environ.setdefault("NCCL_DEBUG", "WARN")
 
 SHAPE = dict(batch=1, length=32768, heads=28, kv_heads=4, head_dim=128)
 SCALE = 128 ** -0.5
