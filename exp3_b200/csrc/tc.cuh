@@ -37,6 +37,17 @@ FPX_INLINE bool mbar_test(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking probe (test_wait never suspends the thread, unlike try_wait).
+FPX_INLINE bool mbar_probe(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Waits for the phase with the given parity to complete. Gives up (returns false) when
 // *abort is set by another role or after kWaitCycles, setting *abort itself then.
 FPX_INLINE bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {

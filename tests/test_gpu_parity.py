@@ -274,3 +274,14 @@ def test_tcgen05_and_mma_exact_kernels_agree():
     torch.testing.assert_close(results[0][0].float(), results[1][0].float(), atol=O_TOL, rtol=0)
     torch.testing.assert_close(results[0][1], results[1][1], atol=LSE_TOL, rtol=0)
     assert _capi.device_error() == 0
+
+
+@pytest.mark.slow
+def test_fused_prefill_divergent_head_lists_32k():
+    """Two query heads of one KV group whose block lists differ a lot (structured routing at 32K):
+    the tensor-core kernel streams the union of both lists, so one tile runs far ahead of the other."""
+    shape = synthetic.LayerShape(1, 32768, 2, 1)
+    q, k, v = synthetic.attention_inputs(shape, seed=13, needles=4, structured_sigma=0.5)
+    sel = run_fused_vs_oracle("mean_native", q, k, v, 0.08, [40, 160, 255])
+    assert not torch.equal(sel[..., 0], sel[..., 1])  # the heads really route differently
+    assert _capi.device_error() == 0
