@@ -134,6 +134,11 @@ def set_exact_kernel(name: str) -> None:
     call("fpx_set_option", 1, {"tcgen05": 0, "mma": 1}[name])
 
 
+def set_route_kernel(name: str) -> None:
+    """Selects the V1 routing kernel: "tcgen05" (the default) or "mma" (the mma.sync cross-check)."""
+    call("fpx_set_option", 3, {"tcgen05": 0, "mma": 1}[name])
+
+
 def set_exp_emulation(pairs_of_8: int) -> None:
     """How many of every 8 exp2 pairs the tcgen05 kernel evaluates on the FMA pipe (0, 2, 3)."""
     call("fpx_set_option", 2, int(pairs_of_8))

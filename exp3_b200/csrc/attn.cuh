@@ -24,10 +24,12 @@ int launch_exact_mma(const ExactParams &p, int mode, int tiles, int heads, int B
 // tcgen05 / TMEM / TMA exact kernel over internal lists (kExactLists).
 int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s);
 
-// Process-wide options (fpx_set_option): which exact kernel the fused path runs, and how many
-// of every 8 exp2 pairs the tcgen05 kernel computes on the FMA pipe (0, 2 or 3).
-enum Option { kOptExactKernel = 1, kOptExpEmulation = 2 };
+// Process-wide options (fpx_set_option): which exact kernel the fused path runs, how many
+// of every 8 exp2 pairs the tcgen05 kernel computes on the FMA pipe (0, 2 or 3), and which
+// V1 routing kernel runs.
+enum Option { kOptExactKernel = 1, kOptExpEmulation = 2, kOptRouteKernel = 3 };
 enum ExactKernel { kExactKernelTcgen05 = 0, kExactKernelMmaSync = 1 };
+enum RouteKernel { kRouteKernelTcgen05 = 0, kRouteKernelMmaSync = 1 };
 int get_option(int key);
 
 enum MeanMode { kMeanMergeInPlace = 0, kMeanStandalone = 1 };

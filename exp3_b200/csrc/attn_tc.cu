@@ -35,6 +35,8 @@
 // their work, so a failed launch ends quickly and the host sees fpx_device_error() != 0.
 #include <cuda.h>
 
+#include <mutex>
+
 #include "attn.cuh"
 #include "tc.cuh"
 
@@ -446,6 +448,8 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+}  // namespace
+
 // [B, rows, heads, 128] bf16 with element strides -> 4-D map (d, head, row, batch), box 64 x 1 x 128 x 1.
 bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int64_t rows, int64_t batch,
                int64_t sh, int64_t sl, int64_t sb) {
@@ -462,6 +466,8 @@ bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+namespace {
 
 template <int kEmu>
 void launch_variant(dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap &tq, const CUtensorMap &tk,
@@ -493,6 +499,20 @@ int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int 
   }
   FPX_CHECK_LAUNCH();
   return FPX_OK;
+}
+
+int *device_error_word() {
+  static std::mutex mu;
+  static int *cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void *ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int *>(ptr);
+  }
+  return cache[dev];
 }
 
 }  // namespace fpx

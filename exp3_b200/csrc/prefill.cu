@@ -72,13 +72,14 @@ extern "C" const char *fpx_status_string(int status) {
 extern "C" int fpx_version(void) { return 1; }
 
 namespace fpx {
-static int g_options[4] = {0, kExactKernelTcgen05, 0, 0};
+static int g_options[4] = {0, kExactKernelTcgen05, 0, kRouteKernelTcgen05};
 int get_option(int key) { return (key > 0 && key < 4) ? g_options[key] : 0; }
 }  // namespace fpx
 
 extern "C" int fpx_set_option(int key, int value) {
   if ((key == kOptExactKernel && (value == kExactKernelTcgen05 || value == kExactKernelMmaSync)) ||
-      (key == kOptExpEmulation && (value == 0 || value == 2 || value == 3))) {
+      (key == kOptExpEmulation && (value == 0 || value == 2 || value == 3)) ||
+      (key == kOptRouteKernel && (value == kRouteKernelTcgen05 || value == kRouteKernelMmaSync))) {
     g_options[key] = value;
     return FPX_OK;
   }
@@ -152,7 +153,7 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
       vp.head_begin = head_begin; vp.tile_begin = tile_begin;
       vp.scale_log2 = (float)scale * kLog2e;
       vp.scores = nullptr; vp.sel = sel;
-      rc = launch_v1_route(vp, tiles, heads, B, s);
+      rc = launch_v1_route_selected(vp, tiles, heads, B, s);
     } else {
       rc = launch_block_stats(st, tile_end, kv_count, B, false, true, s);
       if (rc) return rc;

@@ -6,6 +6,7 @@
 // kernels.py:22-176 (descriptors, selectors, selection, index/mask conversion).
 #include <algorithm>
 
+#include "attn.cuh"
 #include "route.cuh"
 
 namespace fpx {
@@ -238,6 +239,11 @@ __global__ void __launch_bounds__(256) v1_route_kernel(V1Params p) {
 
 size_t v1_route_smem(int nb) {
   return (size_t)(kBlock + kV1Chunk) * kPad * 2 + 2 * 8 * kV1Chunk * 4 + 3 * (size_t)nb * 4 + 64;
+}
+
+int launch_v1_route_selected(const V1Params &p, int tiles, int heads, int B, cudaStream_t s) {
+  return get_option(kOptRouteKernel) == kRouteKernelMmaSync ? launch_v1_route(p, tiles, heads, B, s)
+                                                            : launch_v1_route_tc(p, B, tiles, heads, s);
 }
 
 int launch_v1_route(const V1Params &p, int tiles, int heads, int B, cudaStream_t s) {
@@ -644,7 +650,7 @@ extern "C" int fpx_v1_scores(const void *q, int64_t q_sb, int64_t q_sl, int64_t 
   p.L = L; p.nb = (L + kBlock - 1) / kBlock; p.H = H; p.Hkv = Hkv; p.group = H / Hkv;
   p.scale_log2 = (float)scale * kLog2e;
   p.scores = scores;
-  return launch_v1_route(p, p.nb, H, B, stream);
+  return launch_v1_route_selected(p, p.nb, H, B, stream);
 }
 
 extern "C" int fpx_selector_scores(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,

@@ -55,6 +55,10 @@ struct ColumnSelectParams {
 int launch_block_stats(const StatsParams &p, int blocks, int kv_count, int B, bool bf16_mean,
                        bool desc, cudaStream_t s);
 int launch_v1_route(const V1Params &p, int tiles, int heads, int B, cudaStream_t s);
+// tcgen05 form (route_tc.cu): persistent CTAs over (b, KV group, tile) items.
+int launch_v1_route_tc(const V1Params &p, int B, int tiles, int heads, cudaStream_t s);
+// The kernel fpx_set_option(3, ...) selects.
+int launch_v1_route_selected(const V1Params &p, int tiles, int heads, int B, cudaStream_t s);
 int launch_selector_route(const SelParams &p, int selector, int tiles, int heads, int B,
                           cudaStream_t s);
 int launch_causal_route(const RouteView &r, int H, int head_begin, int heads, int tile_begin,

@@ -149,6 +149,11 @@ FPX_INLINE uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
+FPX_INLINE uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 FPX_INLINE uint64_t fadd2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -245,4 +250,14 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major)
 }
 
 }  // namespace tc
+
+// [B, rows, heads, 128] bf16 with element strides -> 4-D TMA map (d, head, row, batch), box
+// 64 x 1 x 128 x 1, 128-byte swizzle, zero fill outside the tensor (attn_tc.cu).
+bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int64_t rows, int64_t batch,
+               int64_t sh, int64_t sl, int64_t sb);
+
+// Device address of the library's error word (fpx_device_error) on the current device, for
+// kernels in other translation units; null if the runtime cannot resolve it.
+int *device_error_word();
+
 }  // namespace fpx

@@ -276,6 +276,30 @@ def test_tcgen05_and_mma_exact_kernels_agree():
     assert _capi.device_error() == 0
 
 
+@pytest.mark.parametrize("length,heads,kv", [(2049, 14, 2), (32768, 28, 4), (40000, 10, 2)])
+def test_tcgen05_and_mma_route_kernels_agree(length, heads, kv):
+    """The tensor-core V1 routing (transposed products in TMEM, persistent CTAs) against the
+    mma.sync kernel: scores within fp32 rounding, masks bit-exact outside the threshold band.
+    40000 tokens give 313 blocks: items past 256 blocks stream their block means per unit, and
+    the last tile is ragged."""
+    shape = synthetic.LayerShape(1, length, heads, kv)
+    q, k, v = cuda(*synthetic.attention_inputs(shape, seed=length, needles=3, structured_sigma=0.5))
+    mk = upstream.block_mean_k(k)
+    scores, sels = [], []
+    try:
+        for which in ("mma", "tcgen05"):
+            _capi.set_route_kernel(which)
+            scores.append(upstream.v1_scores(q, mk, SCALE).cpu())
+            ops.prefill_attention(q, k, v, "mean_native", 0.08, SCALE)
+            sels.append(ops.export_routing("mean_native", 1, length, heads, kv)[0].cpu())
+    finally:
+        _capi.set_route_kernel("tcgen05")
+    torch.testing.assert_close(scores[1], scores[0], atol=1e-6, rtol=1e-5)
+    blocks = oracle.num_blocks(length)
+    assert_masks_match("mean_native", sels[1], sels[0], scores[0], 0.08, list(range(blocks)))
+    assert _capi.device_error() == 0
+
+
 @pytest.mark.slow
 def test_fused_prefill_divergent_head_lists_32k():
     """Two query heads of one KV group whose block lists differ a lot (structured routing at 32K):
