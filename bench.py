@@ -100,33 +100,82 @@ def exact_pairs(selected, length, kv_range, tile_range, group, block=128):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples during the timed region."""
+    """SM clock and throttle-reason samples taken during the timed region (read only).
+
+    NVML is read every ~2 ms from a thread, so even a region of a few milliseconds gets
+    samples; without NVML it falls back to `nvidia-smi -lms 100`. One sample is also taken
+    synchronously when the region opens (`mark()`)."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index):
-        self.index, self.rows, self.proc = index, [], None
+        self.index, self.rows, self.proc, self.nvml, self.max_mhz = index, [], None, None, None
+        self.stop = threading.Event()
+
+    def _nvml_sample(self):
+        n = self.nvml
+        mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+        bits = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        masks = (n.nvmlClocksEventReasonHwSlowdown, n.nvmlClocksEventReasonHwThermalSlowdown,
+                 n.nvmlClocksEventReasonSwThermalSlowdown, n.nvmlClocksEventReasonSwPowerCap)
+        self.rows.append((float(mhz), {name for name, m in zip(self.REASONS, masks) if bits & m}))
+
+    def _nvml_loop(self):
+        while not self.stop.wait(0.002):
+            try:
+                self._nvml_sample()
+            except Exception:  # a failed read only loses a sample
+                pass
 
     def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.thread = threading.Thread(target=self._nvml_loop, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread = threading.Thread(target=self._smi_read, daemon=True)
             self.thread.start()
         except OSError:
             self.proc = None
         return self
 
-    def _read(self):
+    def mark(self):
+        if self.nvml:
+            try:
+                self._nvml_sample()
+            except Exception:
+                pass
+
+    def _smi_read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                if self.max_mhz is None and parts[2].replace(".", "").isdigit():
+                    self.max_mhz = float(parts[2])
+                self.rows.append((float(parts[1]), {name for name, val in zip(self.REASONS, parts[5:9])
+                                                    if val.lower().startswith("active")}))
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.nvml:
+            self.thread.join(timeout=1)
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc:
             self.proc.terminate()
             try:
@@ -137,16 +186,10 @@ class ClockSampler:
     def summary(self):
         if not self.rows:
             return None
-        mhz = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            for name, val in zip(names, r[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(mhz) if mhz else None,
-                "sm_max_mhz": float(self.rows[0][2]) if self.rows[0][2].replace(".", "").isdigit() else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+        reasons = set().union(*(r for _, r in self.rows))
+        return {"sm_mhz": statistics.median(m for m, _ in self.rows), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.rows),
+                "source": "nvml" if self.nvml else "nvidia-smi"}
 
 
 def cpu_sample_tiles(blocks):
@@ -338,6 +381,7 @@ def main():
         start.record()
         for i in range(args.steps):
             step(ev[i])
+        clocks.mark()  # the steps are queued: the GPU is running them now
         end.record()
         torch.cuda.synchronize()
     if world > 1:

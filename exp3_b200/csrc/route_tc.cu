@@ -105,17 +105,22 @@ FPX_INLINE void block_mass(uint32_t taddr, int nrows, float sl2, float &M, float
 }
 
 struct Item {
-  int b, kvh, t, nblk, chunks;
+  int b, kvh, t, nblk, chunks, h0, h1;  // heads [h0, h1) of the group, as offsets in it
   bool resident;
 };
 
-FPX_INLINE Item item_at(int i, int B, int tiles, int kv_groups, int kv_begin, int tile_begin) {
-  const int per_tile = kv_groups * B;
+// Item i: tile (last - i / (B kv_groups splits)), then batch, then KV group, then the split of
+// the group's G heads into `splits` runs (more items when a launch has few tiles).
+FPX_INLINE Item item_at(int i, int B, int tiles, int kv_groups, int kv_begin, int tile_begin, int G, int splits) {
+  const int per_tile = kv_groups * B * splits;
   const int rank = i / per_tile, rem = i % per_tile;
+  const int sp = rem % splits, rest = rem / splits;
   Item it;
   it.t = tile_begin + tiles - 1 - rank;
-  it.b = rem / kv_groups;
-  it.kvh = kv_begin + rem % kv_groups;
+  it.b = rest / kv_groups;
+  it.kvh = kv_begin + rest % kv_groups;
+  it.h0 = sp * G / splits;
+  it.h1 = (sp + 1) * G / splits;
   it.nblk = it.t + 1;
   it.chunks = (it.nblk + 127) / 128;
   it.resident = it.chunks <= 2;
@@ -124,11 +129,10 @@ FPX_INLINE Item item_at(int i, int B, int tiles, int kv_groups, int kv_begin, in
 
 }  // namespace
 
-// Items run longest tile first: item i is tile (last - i / (B kv_groups)), then batch, then KV
-// group; CTA c takes items c, c + gridDim.x, ...
+// Items run longest tile first; CTA c takes items c, c + gridDim.x, ...
 __global__ void __launch_bounds__(kThreads, 1)
     v1_route_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_mk,
-                       V1Params p, int B, int tiles, int kv_groups, int n_items, int *device_error) {
+                       V1Params p, int B, int tiles, int kv_groups, int splits, int n_items, int *device_error) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   Smem &sh = *reinterpret_cast<Smem *>(smem_raw + pad);
@@ -178,8 +182,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-      const Item it = item_at(i, B, tiles, kv_groups, kv_begin, p.tile_begin);
-      for (int hi = 0; hi < G && ok; ++hi) {
+      const Item it = item_at(i, B, tiles, kv_groups, kv_begin, p.tile_begin, G, splits);
+      for (int hi = it.h0; hi < it.h1 && ok; ++hi) {
         const int s = q_n % kQStages;
         if (q_n >= kQStages && !(ok = mbar_wait_warp(&sh.q_empty[s], (q_n / kQStages - 1) & 1, abort))) break;
         if (lane == 0) {
@@ -190,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ++q_n;
         if (it.resident) {
-          if (hi == 0)
+          if (hi == it.h0)
             for (int c = 0; c < it.chunks && ok; ++c) ok = load_mk(c, it, c);
         } else {
           for (int c = 0; c < it.chunks && ok; ++c) ok = load_mk(mk_rr++ & 1, it, c);
@@ -212,13 +216,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     int q_n = 0, mk_use[2] = {0, 0}, mk_rr = 0, acc_n = 0;
     bool ok = !*abort;
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-      const Item it = item_at(i, B, tiles, kv_groups, kv_begin, p.tile_begin);
-      for (int hi = 0; hi < G && ok; ++hi) {
+      const Item it = item_at(i, B, tiles, kv_groups, kv_begin, p.tile_begin, G, splits);
+      for (int hi = it.h0; hi < it.h1 && ok; ++hi) {
         const int s = q_n % kQStages;
         if (!(ok = mbar_wait_warp(&sh.q_full[s], (q_n / kQStages) & 1, abort))) break;
         for (int c = 0; c < it.chunks && ok; ++c) {
           const int slot = it.resident ? c : (mk_rr & 1);
-          if ((!it.resident || hi == 0) && !(ok = mbar_wait_warp(&sh.mk_full[slot], mk_use[slot] & 1, abort)))
+          if ((!it.resident || hi == it.h0) && !(ok = mbar_wait_warp(&sh.mk_full[slot], mk_use[slot] & 1, abort)))
             break;
           const int a = acc_n % kAcc;
           if (acc_n >= kAcc && !(ok = mbar_wait_warp(&sh.acc_empty[a], (acc_n / kAcc - 1) & 1, abort))) break;
@@ -271,10 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = !*abort;
     auto grp_sync = [&]() { named_sync(1 + g, 128); };
     for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
-      const Item it = item_at(i, B, tiles, kv_groups, kv_begin, p.tile_begin);
+      const Item it = item_at(i, B, tiles, kv_groups, kv_begin, p.tile_begin, G, splits);
       const int t = it.t;
       const int nrows = min(kBlock, p.L - t * kBlock);  // valid query rows of the tile
-      for (int hi = 0; hi < G; ++hi, ++hseq) {
+      for (int hi = it.h0; hi < it.h1; ++hi, ++hseq) {
         if ((hseq & 1) != g) {
           acc_n += it.chunks;
           continue;
@@ -392,6 +396,8 @@ int launch_v1_route_tc(const V1Params &p, int B, int tiles, int heads, cudaStrea
   if (heads % p.group || p.head_begin % p.group) return FPX_ERR_SHAPE;
   if (p.nb > kMaxBlocks) return FPX_ERR_UNSUPPORTED;
   const int kv_groups = heads / p.group;
+  // Split each group's heads over more items when the launch has fewer than two items per SM
+  // (a tile range of one rank, a short sequence): an item's heads run one after another.
   CUtensorMap tq, tmk;
   if (!encode_4d(&tq, p.q, kHeadDim, p.H, p.L, B, p.q_sh, p.q_sl, p.q_sb) ||
       !encode_4d(&tmk, p.mean_k, kHeadDim, p.Hkv, p.nb, B, kHeadDim, (int64_t)p.Hkv * kHeadDim,
@@ -403,11 +409,13 @@ int launch_v1_route_tc(const V1Params &p, int B, int tiles, int heads, cudaStrea
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return FPX_ERR_CUDA;
-  const int n_items = B * tiles * kv_groups;
+  const int base_items = B * tiles * kv_groups;
+  const int splits = std::max(1, std::min(p.group, (2 * sms + base_items - 1) / base_items));
+  const int n_items = base_items * splits;
   const int grid = std::min(n_items, sms);
   const size_t smem = v1_route_tc_smem();
   cudaFuncSetAttribute(v1_route_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  v1_route_tc_kernel<<<grid, kThreads, smem, s>>>(tq, tmk, p, B, tiles, kv_groups, n_items, device_error);
+  v1_route_tc_kernel<<<grid, kThreads, smem, s>>>(tq, tmk, p, B, tiles, kv_groups, splits, n_items, device_error);
   FPX_CHECK_LAUNCH();
   return FPX_OK;
 }

@@ -50,16 +50,18 @@ METHODS = (
 )
 V1_ROUTED_METHODS = {"fp_v1", "mean_native", "fp_v1_rescue", "fp_v1_rescue_v2"}
 MEAN_METHODS = {"mean_native", "mean_balanced", "cgf_mean", "dispersion_mean"}
+RESCUE_METHODS = {"fp_v1_rescue", "fp_v1_rescue_v2"}
 SELECTORS = ("mean_balanced", "cgf_mean", "dispersion_mean")
 
 __all__ = [
-    "BLOCK_SIZE", "METHODS", "V1_ROUTED_METHODS", "MEAN_METHODS", "SELECTORS",
+    "BLOCK_SIZE", "METHODS", "V1_ROUTED_METHODS", "MEAN_METHODS", "RESCUE_METHODS", "SELECTORS",
     "BlockDescriptors", "num_blocks", "f32", "block_mean_k", "v1_scores",
     "deal_output_score", "block_descriptors", "selector_scores",
     "protected_selection", "indices_from_mask", "mask_from_indices",
     "exact_attention", "exact_attention_tiles", "mean_tail", "mean_tail_tiles",
     "merge_exact_mean", "selection_accounting", "dense_attention", "route",
     "prefill_attention_tiles", "exact_token_pairs", "threshold_band",
+    "rescue_choice", "rescue_tail", "rescue_tail_tiles",
 ]
 
 
@@ -376,6 +378,81 @@ def mean_tail(q, desc, selected, scale, block_size=BLOCK_SIZE, chunk_tiles=8):
     return out, lse
 
 
+def rescue_choice(q_tile, k, t, block_size=BLOCK_SIZE):
+    """``kernels.py:276-285`` for one query tile: for every key block kb < t and head h, the
+    token of kb maximising q_mean . k_j, with q_mean the fp32 mean of the tile's valid query
+    rows. Returns int64 [B, H, t] token offsets (ties: the first maximum, as torch.argmax)."""
+    batch, rows, heads, d = q_tile.shape
+    kv_heads = k.shape[2]
+    q_mean = q_tile.float().sum(dim=1) / float(rows)  # [B, H, d]
+    k_blocks = k[:, : t * block_size].float().view(batch, t, block_size, kv_heads, d)
+    scores = torch.einsum("bkgd,bnjkd->bkgnj", q_mean.view(batch, kv_heads, heads // kv_heads, d), k_blocks)
+    return scores.argmax(dim=-1).reshape(batch, heads, t)
+
+
+def _rescue_tile(q_tile, k, v, active_t, t, scale, block_size, remainder, choice=None):
+    """``kernels.py:233-309`` (``rescue_tail``) for one tile: exact attention to one rescue
+    token per unselected block kb < t, and with ``remainder`` the block's other B - 1 tokens
+    through their mean K/V with weight B - 1. fp32 O [B, rows, H, d] and natural LSE."""
+    batch, rows, heads, d = q_tile.shape
+    kv_heads = k.shape[2]
+    group = heads // kv_heads
+    out = torch.zeros(batch, rows, heads, d)
+    lse = torch.full((batch, rows, heads), NEG_INF)
+    if t == 0:
+        return out, lse
+    if choice is None:
+        choice = rescue_choice(q_tile, k, t, block_size)
+    k_blocks = k[:, : t * block_size].float().view(batch, t, block_size, kv_heads, d)
+    v_blocks = v[:, : t * block_size].float().view(batch, t, block_size, kv_heads, d)
+    head_kv = torch.arange(heads) // group
+    bi = torch.arange(batch).view(batch, 1, 1)
+    ni = torch.arange(t).view(1, 1, t)
+    ki = head_kv.view(1, heads, 1)
+    k_res = k_blocks[bi, ni, choice, ki]  # [B, H, t, d]
+    v_res = v_blocks[bi, ni, choice, ki]
+    tail = (~active_t[:, :t, :]).permute(0, 2, 1)  # [B, H, t]
+    qf = q_tile.float()
+    logits = torch.einsum("brhd,bhnd->brhn", qf, k_res) * scale
+    values = v_res
+    mask = tail.unsqueeze(1)
+    if remainder:
+        k_sum = k_blocks.sum(dim=2)[:, :, head_kv].permute(0, 2, 1, 3)  # [B, H, t, d]
+        v_sum = v_blocks.sum(dim=2)[:, :, head_kv].permute(0, 2, 1, 3)
+        k_rest = (k_sum - k_res) / (block_size - 1)
+        v_rest = (v_sum - v_res) / (block_size - 1)
+        rest = torch.einsum("brhd,bhnd->brhn", qf, k_rest) * scale
+        logits = torch.cat((logits, rest + math.log(block_size - 1)), dim=-1)
+        values = torch.cat((values, v_rest), dim=2)
+        mask = torch.cat((mask, mask), dim=-1)
+    masked = logits.masked_fill(~mask, NEG_INF)
+    lse = torch.logsumexp(masked, dim=-1)
+    weights = torch.where(mask, torch.exp(masked - lse.unsqueeze(-1)), 0.0)
+    out = torch.einsum("brhn,bhnd->brhd", weights, values)
+    return out, lse
+
+
+def rescue_tail_tiles(q, k, v, selected, scale, remainder=False, block_size=BLOCK_SIZE, tiles=None):
+    """``kernels.py:233-309`` over the tiles in ``tiles``: dict t -> (O fp32, LSE fp32)."""
+    length = q.shape[1]
+    blocks = num_blocks(length, block_size)
+    result = {}
+    for t in range(blocks) if tiles is None else tiles:
+        lo, hi = _tile_rows(t, length, block_size)
+        result[t] = _rescue_tile(q[:, lo:hi], k, v, selected[:, t], t, scale, block_size, remainder)
+    return result
+
+
+def rescue_tail(q, k, v, selected, scale, block_size=BLOCK_SIZE, remainder=False):
+    """``kernels.py:233-309``: fp32 O [B, L, H, d] and LSE [B, L, H] of the rescue entries."""
+    out = torch.zeros(q.shape, dtype=torch.float32)
+    lse = torch.full(q.shape[:3], NEG_INF, dtype=torch.float32)
+    for t, (o_t, l_t) in rescue_tail_tiles(q, k, v, selected, scale, remainder, block_size).items():
+        lo, hi = _tile_rows(t, q.shape[1], block_size)
+        out[:, lo:hi], lse[:, lo:hi] = o_t, l_t
+    return out, lse
+
+
 def merge_exact_mean(exact_output, exact_lse, mean_output, mean_lse):
     """``kernels.py:312-325``: logaddexp merge; the exact output enters at its stored dtype."""
     total_lse = torch.logaddexp(exact_lse, mean_lse)
@@ -513,7 +590,7 @@ def prefill_attention_tiles(method, q, k, v, scale, alpha, sink=2, window=4, las
     Mean methods merge the exact path (stored bf16, ``kernels.py:322``) with the
     block-mean tail. ``routing`` may pass a precomputed (selected, scores, desc).
     """
-    if method not in METHODS or method in {"fp_v1_rescue", "fp_v1_rescue_v2"}:
+    if method not in METHODS:
         raise ValueError(f"unsupported method {method!r}")
     selected, scores, desc = routing or route(method, q, k, v, scale, alpha, sink, window, last_full,
                                               block_size, tiles)
@@ -521,10 +598,14 @@ def prefill_attention_tiles(method, q, k, v, scale, alpha, sink=2, window=4, las
     outputs = {}
     for t, (o_e, l_e) in exact.items():
         o_e = o_e.to(q.dtype)
+        lo, hi = _tile_rows(t, q.shape[1], block_size)
         if method in MEAN_METHODS:
-            lo, hi = _tile_rows(t, q.shape[1], block_size)
             o_m, l_m = _mean_tile(q[:, lo:hi], desc, selected[:, t], t, scale)
             outputs[t] = merge_exact_mean(o_e, l_e, o_m, l_m)
+        elif method in RESCUE_METHODS:  # attention.py:306-331
+            o_r, l_r = _rescue_tile(q[:, lo:hi], k, v, selected[:, t], t, scale, block_size,
+                                    method == "fp_v1_rescue_v2")
+            outputs[t] = merge_exact_mean(o_e, l_e, o_r, l_r)
         else:
             outputs[t] = (o_e, l_e)
     return outputs, selected, scores

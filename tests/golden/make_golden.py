@@ -7,7 +7,8 @@ the first argument, default ``/root/reference``); the GPU box never runs this.
 
 What runs, all on the CPU in fp32:
 - the reference's torch functions in ``kernels.py`` (descriptors, selectors,
-  protected selection, index/mask conversion, mean tail, merge, accounting);
+  protected selection, index/mask conversion, mean tail, rescue tails, merge,
+  accounting);
 - the reference's Triton kernels in ``upstream/flashprefill_native_forward.py``
   under ``TRITON_INTERPRET=1`` (``compute_mean_vector``, ``compute_block_score``,
   ``_flash_forward`` called through ``.fn[grid]`` with fixed tile sizes, which
@@ -172,7 +173,24 @@ def main(root="/root/reference"):
         record[f"{selector}_indices"] = i.numpy()
         record[f"{selector}_counts"] = c.numpy()
     np.savez_compressed(HERE / "selectors_l385.npz", **record)
-    for name in ("v1_routing_l1089.npz", "exact_mean_l257.npz", "selectors_l385.npz"):
+    # Case 4: the rescue tails (kernels.py:233-309) of fp_v1_rescue / _v2, L=1153 (10 blocks, the
+    # last with one row), on a random protected selection with narrow protection so tiles have
+    # tails. O is stored on every 9th row (fp32 outputs are large), the LSE on all rows.
+    seed, length, heads, kv_heads = 29, 1153, 4, 2
+    q, k, v = inputs(seed, length, heads, kv_heads)
+    q32, k32, v32 = q.float(), k.float(), v.float()
+    blocks = 10
+    g = torch.Generator().manual_seed(seed)
+    selected = kernels.protected_selection(torch.rand(1, blocks, blocks, heads, generator=g), 0.6, 1, 1, 1)
+    record = {"seed": seed, "length": length, "heads": heads, "kv_heads": kv_heads,
+              "digest": synthetic.tensor_digest(q, k, v), "selected": selected.numpy(),
+              "rows": np.arange(0, length, 9)}
+    for name, remainder in (("rescue", False), ("rescue_v2", True)):
+        o, lse = kernels.rescue_tail(q32, k32, v32, selected, SCALE, chunk_tiles=3, remainder=remainder)
+        record[f"{name}_out_rows"] = o[:, ::9].numpy()
+        record[f"{name}_lse"] = lse.numpy()
+    np.savez_compressed(HERE / "rescue_l1153.npz", **record)
+    for name in ("v1_routing_l1089.npz", "exact_mean_l257.npz", "selectors_l385.npz", "rescue_l1153.npz"):
         print(name, (HERE / name).stat().st_size, "bytes")
 
 

@@ -105,3 +105,14 @@ def test_unknown_selector_raises():
     except ValueError:
         return
     raise AssertionError("unknown selector accepted")
+
+
+def test_rescue_tails_match_reference():
+    data, q, k, v = load("rescue_l1153.npz")
+    selected = t(data["selected"])
+    rows = t(data["rows"])
+    assert (~selected).any()  # the fixture's tiles have tails
+    for name, remainder in (("rescue", False), ("rescue_v2", True)):
+        out, lse = oracle.rescue_tail(q, k, v, selected, SCALE, remainder=remainder)
+        torch.testing.assert_close(lse, t(data[f"{name}_lse"]), atol=1e-5, rtol=1e-5)
+        torch.testing.assert_close(out[:, rows], t(data[f"{name}_out_rows"]), atol=1e-5, rtol=1e-5)
