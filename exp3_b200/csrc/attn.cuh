@@ -25,11 +25,12 @@ int launch_exact_mma(const ExactParams &p, int mode, int tiles, int heads, int B
 int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s);
 
 // Process-wide options (fpx_set_option): which exact kernel the fused path runs, how many
-// of every 8 exp2 pairs the tcgen05 kernel computes on the FMA pipe (0, 2 or 3), and which
-// V1 routing kernel runs.
-enum Option { kOptExactKernel = 1, kOptExpEmulation = 2, kOptRouteKernel = 3 };
+// of every 8 exp2 pairs the tcgen05 kernel computes on the FMA pipe (0, 2 or 3), which V1
+// routing kernel runs and which mean-tail kernel runs.
+enum Option { kOptExactKernel = 1, kOptExpEmulation = 2, kOptRouteKernel = 3, kOptMeanKernel = 4 };
 enum ExactKernel { kExactKernelTcgen05 = 0, kExactKernelMmaSync = 1 };
 enum RouteKernel { kRouteKernelTcgen05 = 0, kRouteKernelMmaSync = 1 };
+enum MeanKernel { kMeanKernelTcgen05 = 0, kMeanKernelFp32 = 1 };
 int get_option(int key);
 
 enum MeanMode { kMeanMergeInPlace = 0, kMeanStandalone = 1 };
@@ -38,6 +39,9 @@ struct MeanParams {
   const __nv_bfloat16 *q;
   int64_t q_sb, q_sl, q_sh;
   const float *mean_k, *mean_v;     // [B][nb][Hkv][d]
+  // bf16 splits of the same descriptors for the tensor-core tail: mean_k = mk_hi + mk_lo
+  // (lo = bf16 of the rounding remainder), mv_hi = bf16(mean_v)
+  const __nv_bfloat16 *mk_hi, *mk_lo, *mv_hi;
   int L, nb, H, Hkv, group, head_begin, tile_begin;
   float scale;
   RouteView route;                  // kMeanMergeInPlace: tail bits
@@ -51,6 +55,8 @@ struct MeanParams {
 };
 
 int launch_mean_tail(const MeanParams &p, int mode, int tiles, int heads, int B, cudaStream_t s);
+// tcgen05 / TMEM / TMA tail, merged in place (attn_tail_tc.cu); needs mk_hi, mk_lo, mv_hi.
+int launch_mean_tail_tc(const MeanParams &p, int B, int tiles, int heads, cudaStream_t s);
 int launch_merge(const __nv_bfloat16 *exact_out, const float *exact_lse, const float *mean_out,
                  const float *mean_lse, int64_t rows, __nv_bfloat16 *out, float *lse,
                  cudaStream_t s);

@@ -14,7 +14,7 @@ namespace fpx {
 struct Workspace {
   int32_t *lists, *counts;
   uint32_t *tail;
-  __nv_bfloat16 *mk16;
+  __nv_bfloat16 *mk16, *mkh, *mkl, *mvh;
   float *mk, *mv, *vk, *sv, *lse;
   size_t bytes;
 };
@@ -35,6 +35,9 @@ static Workspace carve(void *base, int B, int L, int H, int Hkv) {
   w.tail = reinterpret_cast<uint32_t *>(take((size_t)B * H * nb * words * 4));
   const size_t desc = (size_t)B * nb * Hkv * kHeadDim;
   w.mk16 = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
+  w.mkh = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
+  w.mkl = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
+  w.mvh = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
   w.mk = reinterpret_cast<float *>(take(desc * 4));
   w.mv = reinterpret_cast<float *>(take(desc * 4));
   w.vk = reinterpret_cast<float *>(take(desc * 4));
@@ -72,14 +75,15 @@ extern "C" const char *fpx_status_string(int status) {
 extern "C" int fpx_version(void) { return 1; }
 
 namespace fpx {
-static int g_options[4] = {0, kExactKernelTcgen05, 0, kRouteKernelTcgen05};
-int get_option(int key) { return (key > 0 && key < 4) ? g_options[key] : 0; }
+static int g_options[5] = {0, kExactKernelTcgen05, 0, kRouteKernelTcgen05, kMeanKernelTcgen05};
+int get_option(int key) { return (key > 0 && key < 5) ? g_options[key] : 0; }
 }  // namespace fpx
 
 extern "C" int fpx_set_option(int key, int value) {
   if ((key == kOptExactKernel && (value == kExactKernelTcgen05 || value == kExactKernelMmaSync)) ||
       (key == kOptExpEmulation && (value == 0 || value == 2 || value == 3)) ||
-      (key == kOptRouteKernel && (value == kRouteKernelTcgen05 || value == kRouteKernelMmaSync))) {
+      (key == kOptRouteKernel && (value == kRouteKernelTcgen05 || value == kRouteKernelMmaSync)) ||
+      (key == kOptMeanKernel && (value == kMeanKernelTcgen05 || value == kMeanKernelFp32))) {
     g_options[key] = value;
     return FPX_OK;
   }
@@ -142,6 +146,7 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     st.L = L; st.nb = nb; st.Hkv = Hkv; st.kv_begin = kv_begin;
     st.mean_bf16 = ws.mk16; st.mean_k = ws.mk; st.mean_v = ws.mv; st.var_k = ws.vk;
     st.sigma_v = ws.sv; st.counts = nullptr;
+    st.mk_hi = ws.mkh; st.mk_lo = ws.mkl; st.mv_hi = ws.mvh;
     if (method == FPX_METHOD_DENSE) {
       rc = launch_causal_route(rv, H, head_begin, heads, tile_begin, tiles, B, s);
     } else if (method == FPX_METHOD_FP_V1 || method == FPX_METHOD_MEAN_NATIVE) {
@@ -192,12 +197,14 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     MeanParams mp{};
     mp.q = qb; mp.q_sb = q_sb; mp.q_sl = q_sl; mp.q_sh = q_sh;
     mp.mean_k = ws.mk; mp.mean_v = ws.mv;
+    mp.mk_hi = ws.mkh; mp.mk_lo = ws.mkl; mp.mv_hi = ws.mvh;
     mp.L = L; mp.nb = nb; mp.H = H; mp.Hkv = Hkv; mp.group = G;
     mp.head_begin = head_begin; mp.tile_begin = tile_begin;
     mp.scale = (float)scale; mp.route = rv;
     mp.out = static_cast<__nv_bfloat16 *>(out); mp.o_sb = o_sb; mp.o_sl = o_sl; mp.o_sh = o_sh;
     mp.lse = lse_out;
-    rc = launch_mean_tail(mp, kMeanMergeInPlace, tiles, heads, B, s);
+    rc = get_option(kOptMeanKernel) == kMeanKernelFp32 ? launch_mean_tail(mp, kMeanMergeInPlace, tiles, heads, B, s)
+                                                       : launch_mean_tail_tc(mp, B, tiles, heads, s);
   }
   return rc;
 }

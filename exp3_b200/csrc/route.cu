@@ -46,6 +46,12 @@ __global__ void __launch_bounds__(128) block_stats_kernel(StatsParams p) {
     p.mean_k[o] = mk;
     p.var_k[o] = fmaxf(__fsub_rn(__fdiv_rn(sk2, fn), __fmul_rn(mk, mk)), 0.f);
     p.mean_v[o] = mv;
+    if (p.mk_hi) {  // mean_k = hi + lo exactly up to lo's rounding; the remainder is exact in fp32
+      const __nv_bfloat16 hi = __float2bfloat16_rn(mk);
+      p.mk_hi[o] = hi;
+      p.mk_lo[o] = __float2bfloat16_rn(__fsub_rn(mk, __bfloat162float(hi)));
+      p.mv_hi[o] = __float2bfloat16_rn(mv);
+    }
     const float var_v = fmaxf(__fsub_rn(__fdiv_rn(sv2, fn), __fmul_rn(mv, mv)), 0.f);
     const float total = block_sum<128>(var_v, red);
     if (c == 0) p.sigma_v[((int64_t)b * p.nb + blk) * p.Hkv + kvh] = sqrtf(total);

@@ -11,6 +11,7 @@ struct StatsParams {
   int L, nb, Hkv, kv_begin;
   __nv_bfloat16 *mean_bf16;                      // [B][nb][Hkv][d] (V1 block mean)
   float *mean_k, *mean_v, *var_k, *sigma_v;      // fp32 descriptors
+  __nv_bfloat16 *mk_hi, *mk_lo, *mv_hi;          // bf16 splits for the tensor-core tail, or null
   int32_t *counts;                               // [nb] or null
 };
 
