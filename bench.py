@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--method mean_native] [--alpha 0.08] [--variant iid|structured]
+                    [--config c2|c4|c5] [--workload layer|model]
 
 One step = one attention layer (route -> exact -> mean + merge) over B=1, L=32768,
 H=28, Hkv=4, d=128 synthetic inputs (N(0,1) + RoPE theta 1e6 + 32 needles) already
@@ -11,6 +12,8 @@ over the max-over-ranks step time. With N GPUs (torchrun) the layer's independen
 units — (KV group, query-tile range) — are split across ranks with no collective in the
 data path (strong scaling). ``--impl reference`` times the reference algorithm's CPU
 restatement (oracle/) on this host's cores on a bounded sample of the same layer.
+``--config c4|c5`` runs the 128K layer or the Qwen2.5-32B-shape (B=2, 64K) layer the same way;
+``--workload model`` runs the full-model prefill + decode of config 3 (tensor parallel).
 """
 
 from __future__ import annotations
@@ -33,11 +36,25 @@ sys.path.insert(0, str(ROOT))
 # Keep rank 0's stdout to the one JSON line (NCCL otherwise announces its version there).
 os.environ.setdefault("NCCL_DEBUG", "WARN")
 
-SHAPE = dict(batch=1, length=32768, heads=28, kv_heads=4, head_dim=128)
 SCALE = 128 ** -0.5
-METRIC = "effective TFLOP/s of the 32K Qwen2.5-7B-shape prefill attention layer"
-WORKLOAD = ("config 2: one attention layer, B=1 L=32768 H=28 Hkv=4 d=128 bf16, synthetic N(0,1) Q/K/V + "
-            "RoPE(theta 1e6) + 32 needles")
+# Layer workloads (--config): c2 is the headline; c4 / c5 are BASELINE.json's long-sequence and
+# 32B-shape layers, sharded the same way.
+LAYER_CONFIGS = {
+    "c2": dict(batch=1, length=32768, heads=28, kv_heads=4,
+               metric="effective TFLOP/s of the 32K Qwen2.5-7B-shape prefill attention layer",
+               workload="config 2: one attention layer, B=1 L=32768 H=28 Hkv=4 d=128 bf16, synthetic N(0,1) "
+                        "Q/K/V + RoPE(theta 1e6) + 32 needles"),
+    "c4": dict(batch=1, length=131072, heads=28, kv_heads=4,
+               metric="effective TFLOP/s of the 128K Qwen2.5-7B-shape prefill attention layer",
+               workload="config 4: one attention layer, B=1 L=131072 H=28 Hkv=4 d=128 bf16, synthetic N(0,1) "
+                        "Q/K/V + RoPE(theta 1e6) + 128 needles"),
+    "c5": dict(batch=2, length=65536, heads=40, kv_heads=8,
+               metric="effective TFLOP/s of the 64K Qwen2.5-32B-shape prefill attention layer",
+               workload="config 5: one attention layer, B=2 L=65536 H=40 Hkv=8 d=128 bf16, synthetic N(0,1) "
+                        "Q/K/V + RoPE(theta 1e6), K row norms log-normal(0, 0.5)"),
+}
+METRIC = LAYER_CONFIGS["c2"]["metric"]
+WORKLOAD = LAYER_CONFIGS["c2"]["workload"]
 
 
 def parse():
@@ -50,6 +67,8 @@ def parse():
     ap.add_argument("--alpha", type=float, default=0.08)
     ap.add_argument("--variant", default="iid", choices=["iid", "structured"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default="c2", choices=sorted(LAYER_CONFIGS),
+                    help="layer workload: c2 (32K, the headline), c4 (128K), c5 (32B shape, B=2, 64K)")
     ap.add_argument("--workload", default="layer", choices=["layer", "model"],
                     help="layer: the 32K attention layer (default); model: full-model prefill + decode")
     ap.add_argument("--prompt-length", type=int, default=32640)
@@ -65,10 +84,10 @@ def peaks():
         return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def inputs(variant, device):
+def inputs(variant, device, config="c2"):
     from exp3_b200 import synthetic
     kw = {"structured_sigma": 0.5} if variant == "structured" else {}
-    return synthetic.config_inputs("c2", seed=0, device=device, **kw)
+    return synthetic.config_inputs(config, seed=0, device=device, **kw)
 
 
 def partition(rank, world, kv_heads, blocks):
@@ -336,10 +355,11 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    b, length, heads, kv_heads, d = (SHAPE[x] for x in ("batch", "length", "heads", "kv_heads", "head_dim"))
+    cfg = LAYER_CONFIGS[args.config]
+    b, length, heads, kv_heads, d = cfg["batch"], cfg["length"], cfg["heads"], cfg["kv_heads"], 128
     group = heads // kv_heads
     blocks = length // 128
-    q, k, v = inputs(args.variant, dev)
+    q, k, v = inputs(args.variant, dev, args.config)
     kv_range, tile_range = partition(rank, world, kv_heads, blocks)
     method, alpha = args.method, args.alpha
     nbytes = ops.workspace_bytes(method, b, length, heads, kv_heads)
@@ -460,17 +480,17 @@ def main():
     line = None
     if rank == 0:
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and args.config == "c2":
             qc, kc, vc = q.cpu(), k.cpu(), v.cpu()
             cpu = cpu_baseline(method, alpha, qc, kc, vc)
         line = {
-            "metric": METRIC, "value": total_flops / (ms_step * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "metric": cfg["metric"], "value": total_flops / (ms_step * 1e-3) / 1e12, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "method": method, "alpha": alpha, "variant": args.variant,
+            "config": {"workload": cfg["workload"], "method": method, "alpha": alpha, "variant": args.variant,
                        "ms_per_layer": ms_step, "density": density, "exact_token_pairs": all_pairs,
-                       "l2": "no flush: Q (235 MB) and O are larger than the 126 MB L2",
+                       "l2": f"no flush: Q ({q.numel() * 2 / 1e6:.0f} MB) and O are larger than the 126 MB L2",
                        "parallelism": f"{world} rank(s): (KV group x query-tile range) shards, no collective",
                        "stage_ms_rank0": {"route": route_ms, "exact": exact_ms, "mean_merge": mean_ms}},
             "roofline": {"bound": "tensor", "kernel": "exact attention (sparse FA)", "achieved": achieved,

@@ -549,12 +549,15 @@ __global__ void __launch_bounds__(128) export_routing_kernel(RouteView r, int H,
                                                              int64_t *indices, int32_t *counts) {
   const int t = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int64_t rrow = r.row(b, h, t, H);
-  const int cnt = r.counts[rrow];
+  // Clamped: a workspace whose routing was cut short by a failed launch holds stale values.
+  const int cnt = min(max(r.counts[rrow], 0), r.nb);
   const int64_t col = ((int64_t)b * r.nb + t) * r.nb * H + h;
   const int32_t *list = r.lists + rrow * r.nb;
   for (int j = threadIdx.x; j < r.nb; j += blockDim.x) {
-    if (indices) indices[col + (int64_t)j * H] = j < cnt ? list[j] : r.nb;
-    if (mask && j < cnt) mask[col + (int64_t)list[j] * H] = 1;
+    const int kb = j < cnt ? list[j] : r.nb;
+    const bool valid = kb >= 0 && kb < r.nb;
+    if (indices) indices[col + (int64_t)j * H] = valid ? kb : r.nb;
+    if (mask && valid) mask[col + (int64_t)kb * H] = 1;
   }
   if (counts && threadIdx.x == 0) counts[((int64_t)b * r.nb + t) * H + h] = cnt;
 }

@@ -37,7 +37,8 @@ using namespace tc;
 
 constexpr int kThreads = 320;
 constexpr int kQStages = 3;
-constexpr int kAcc = 4;                   // 128-column accumulators in 512 TMEM columns
+constexpr int kAcc = 4;                   // 128-column accumulators in 512 TMEM columns:
+                                          // slots 2g, 2g + 1 belong to epilogue warpgroup g
 constexpr int kMaxBlocks = 2048;          // L <= 262144
 constexpr uint32_t kHalf = 128 * 128;     // 128 rows x 64 bf16, one SW128 half tile
 constexpr uint32_t kTile = 2 * kHalf;     // 128 x 128 bf16
@@ -213,19 +214,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    int q_n = 0, mk_use[2] = {0, 0}, mk_rr = 0, acc_n = 0;
+    // Each warpgroup's two slots are filled and drained strictly in turn, so no wait on a slot is
+    // ever more than one phase ahead of it (a parity wait cannot tell phases two apart).
+    int q_n = 0, mk_use[2] = {0, 0}, mk_rr = 0, issued[2] = {0, 0}, hseq = 0;
     bool ok = !*abort;
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
       const Item it = item_at(i, B, tiles, kv_groups, kv_begin, p.tile_begin, G, splits);
-      for (int hi = it.h0; hi < it.h1 && ok; ++hi) {
+      for (int hi = it.h0; hi < it.h1 && ok; ++hi, ++hseq) {
+        const int g = hseq & 1;  // the warpgroup that reduces this head
         const int s = q_n % kQStages;
         if (!(ok = mbar_wait_warp(&sh.q_full[s], (q_n / kQStages) & 1, abort))) break;
         for (int c = 0; c < it.chunks && ok; ++c) {
           const int slot = it.resident ? c : (mk_rr & 1);
           if ((!it.resident || hi == it.h0) && !(ok = mbar_wait_warp(&sh.mk_full[slot], mk_use[slot] & 1, abort)))
             break;
-          const int a = acc_n % kAcc;
-          if (acc_n >= kAcc && !(ok = mbar_wait_warp(&sh.acc_empty[a], (acc_n / kAcc - 1) & 1, abort))) break;
+          const int a = 2 * g + (issued[g] & 1), use = issued[g] >> 1;
+          if (use > 0 && !(ok = mbar_wait_warp(&sh.acc_empty[a], (use - 1) & 1, abort))) break;
           tc_fence_after();
           if (lane == 0) {
 #pragma unroll
@@ -240,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++mk_use[slot];
             ++mk_rr;
           }
-          ++acc_n;
+          ++issued[g];
         }
         if (!ok) break;
         if (lane == 0) tc_commit(&sh.q_empty[s]);
@@ -271,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale_log2;
     const SelectArgs &a = p.sel;
     float *bm = sh.bm[g], *bs = sh.bs[g], *sc = sh.sc[g];
-    int acc_n = 0, hseq = 0, red_k = 0;
+    int done = 0, hseq = 0, red_k = 0;  // done: units this warpgroup has reduced
     bool ok = !*abort;
     auto grp_sync = [&]() { named_sync(1 + g, 128); };
     for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
@@ -279,14 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t = it.t;
       const int nrows = min(kBlock, p.L - t * kBlock);  // valid query rows of the tile
       for (int hi = it.h0; hi < it.h1; ++hi, ++hseq) {
-        if ((hseq & 1) != g) {
-          acc_n += it.chunks;
-          continue;
-        }
+        if ((hseq & 1) != g) continue;
         const int h = it.kvh * G + hi;
-        for (int c = 0; c < it.chunks; ++c, ++acc_n) {
-          const int ac = acc_n % kAcc;
-          if (ok) ok = mbar_wait_warp(&sh.acc_full[ac], (acc_n / kAcc) & 1, abort);
+        for (int c = 0; c < it.chunks; ++c, ++done) {
+          const int ac = 2 * g + (done & 1);
+          if (ok) ok = mbar_wait_warp(&sh.acc_full[ac], (done >> 1) & 1, abort);
           tc_fence_after();
           const int kb = c * 128 + e;
           const uint32_t taddr = tmem + lane_off + 128 * ac;
@@ -315,14 +316,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         // handles blocks e, e + 128, ...: the same blocks it wrote above, so bm / bs / sc need
         // no barrier of their own. score = r / total with r = S exp2(M - max M); max score is
         // (max r) / total exactly, as rounding is monotonic.
+        // The group agrees on whether every warp's waits succeeded before anything is written,
+        // so a row is either complete or has count 0 (never a count over unwritten entries).
         float lm = -INFINITY;
         for (int kb = e; kb < it.nblk; kb += 128) lm = fmaxf(lm, bm[kb]);
         lm = warp_max(lm);
         float *red = sh.red[g][red_k & 1];
-        if (lane == 0) red[ew] = lm;
+        if (lane == 0) {
+          red[ew] = lm;
+          red[4 + ew] = ok ? 1.f : 0.f;
+        }
         grp_sync();
         ++red_k;
         const float gmax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+        const bool wg_ok = (red[4] + red[5]) + (red[6] + red[7]) == 4.f;
         float ls = 0.f, lr = 0.f;
         for (int kb = e; kb < it.nblk; kb += 128) {
           const float m = bm[kb];
@@ -342,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++red_k;
         const float total = ((red[0] + red[1]) + (red[2] + red[3])) + 1e-9f;
         const float smax = fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])) / total;
-        if (p.scores && ok)
+        if (p.scores && wg_ok)
           for (int kb = e; kb < p.nb; kb += 128)
             p.scores[(((int64_t)it.b * p.nb + t) * p.nb + kb) * p.H + h] = kb < it.nblk ? sc[kb] / total : 0.f;
         if (a.route.lists) {
@@ -370,12 +377,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const unsigned bal = __ballot_sync(0xffffffffu, active);
             int pre = 0;
             for (int w = 0; w < ew; ++w) pre += cnt[4 * j + w];
-            if (active && ok) list[base + pre + __popc(bal & ((1u << lane) - 1u))] = kb;
+            if (active && wg_ok) list[base + pre + __popc(bal & ((1u << lane) - 1u))] = kb;
             const unsigned tb = __ballot_sync(0xffffffffu, kb < a.nb && kb < t && !active);
-            if (lane == 0 && kb < a.nb && ok) tail[kb >> 5] = tb;
+            if (lane == 0 && kb < a.nb && wg_ok) tail[kb >> 5] = tb;
             base += (cnt[4 * j] + cnt[4 * j + 1]) + (cnt[4 * j + 2] + cnt[4 * j + 3]);
           }
-          if (e == 0 && ok) a.route.counts[rrow] = base;
+          if (e == 0) a.route.counts[rrow] = wg_ok ? base : 0;
         }
       }
     }

@@ -19,6 +19,7 @@ from __future__ import annotations
 import hashlib
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 
@@ -46,20 +47,44 @@ def generator(seed: int, device="cpu") -> torch.Generator:
     return g
 
 
+def _np_rng(seed: int) -> np.random.Generator:
+    return np.random.Generator(np.random.PCG64(seed))
+
+
 def randn_bf16(shape, seed: int, device="cpu") -> torch.Tensor:
-    """N(0, 1) rounded to bf16, from a seeded generator on ``device``."""
-    return torch.randn(shape, generator=generator(seed, device), device=device,
-                       dtype=torch.float32).to(torch.bfloat16)
+    """N(0, 1) rounded to bf16.
+
+    On the CPU the draws come from numpy's PCG64 stream in float64 (generated in slices, so
+    memory stays bounded) and are rounded to fp32 and then bf16: the bits are the same on
+    every x86-64 host, which the golden fixtures rely on (torch's CPU sampler uses vectorised
+    fp32 math whose last bits depend on the instruction set). On a GPU the device's own
+    generator is used (fast, deterministic for a given GPU type)."""
+    if torch.device(device).type != "cpu":
+        return torch.randn(shape, generator=generator(seed, device), device=device,
+                           dtype=torch.float32).to(torch.bfloat16)
+    out = torch.empty(shape, dtype=torch.bfloat16)
+    flat = out.view(-1)
+    rng = _np_rng(seed)
+    step = 1 << 24
+    for lo in range(0, flat.numel(), step):
+        n = min(step, flat.numel() - lo)
+        flat[lo:lo + n] = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).to(torch.bfloat16)
+    return out
+
+
+def rope_tables(length: int, d: int, theta: float = 1e6, offset: int = 0):
+    """fp32 cos / sin [length, d] of NeoX RoPE, evaluated in float64 and rounded once."""
+    inv_freq = 1.0 / (theta ** (np.arange(0, d, 2, dtype=np.float64) / d))
+    freqs = np.outer(np.arange(offset, offset + length, dtype=np.float64), inv_freq)
+    emb = np.concatenate((freqs, freqs), axis=-1)
+    return torch.from_numpy(np.cos(emb).astype(np.float32)), torch.from_numpy(np.sin(emb).astype(np.float32))
 
 
 def rope(x: torch.Tensor, theta: float = 1e6, offset: int = 0) -> torch.Tensor:
     """NeoX half-rotation RoPE on [B, L, H, d] (HF Qwen2 ``apply_rotary_pos_emb``)."""
     d = x.shape[-1]
-    inv_freq = 1.0 / (theta ** (torch.arange(0, d, 2, device=x.device, dtype=torch.float32) / d))
-    pos = torch.arange(offset, offset + x.shape[1], device=x.device, dtype=torch.float32)
-    freqs = torch.outer(pos, inv_freq)
-    emb = torch.cat((freqs, freqs), dim=-1)
-    cos, sin = emb.cos()[None, :, None, :], emb.sin()[None, :, None, :]
+    cos, sin = rope_tables(x.shape[1], d, theta, offset)
+    cos, sin = cos.to(x.device)[None, :, None, :], sin.to(x.device)[None, :, None, :]
     xf = x.float()
     half = d // 2
     rotated = torch.cat((-xf[..., half:], xf[..., :half]), dim=-1)
@@ -74,26 +99,27 @@ def attention_inputs(shape: LayerShape, seed: int = 0, needles: int = 0, device=
     q = randn_bf16((b, length, h, d), seed, device)
     k = randn_bf16((b, length, hkv, d), seed + 1, device)
     v = randn_bf16((b, length, hkv, d), seed + 2, device)
-    g = generator(seed + 3, "cpu")
+    rng = _np_rng(seed + 3)
     group = h // hkv
     if structured_sigma > 0:
         blocks = (length + 127) // 128
-        direction = torch.randn(b, 1, hkv, d, generator=g)
-        direction = direction / direction.norm(dim=-1, keepdim=True) * d ** 0.5
-        offsets = torch.randn(b, blocks, hkv, 1, generator=g) * structured_sigma
-        shift = (offsets * direction).repeat_interleave(128, dim=1)[:, :length]
+        direction = rng.standard_normal((b, 1, hkv, d))
+        direction = direction / np.linalg.norm(direction, axis=-1, keepdims=True) * d ** 0.5
+        offsets = rng.standard_normal((b, blocks, hkv, 1)) * structured_sigma
+        shift = torch.from_numpy((offsets * direction).astype(np.float32))
+        shift = shift.repeat_interleave(128, dim=1)[:, :length]
         k = (k.float() + shift.to(device)).to(torch.bfloat16)
-        lean = direction.repeat_interleave(group, dim=2) * 0.25
+        lean = torch.from_numpy((direction * 0.25).astype(np.float32)).repeat_interleave(group, dim=2)
         q = (q.float() + lean.to(device)).to(torch.bfloat16)
     if key_lognormal_sigma > 0:
-        norms = torch.exp(torch.randn(b, length, hkv, 1, generator=g) * key_lognormal_sigma)
-        k = (k.float() * norms.to(device)).to(torch.bfloat16)
+        norms = np.exp(rng.standard_normal((b, length, hkv, 1)) * key_lognormal_sigma)
+        k = (k.float() * torch.from_numpy(norms.astype(np.float32)).to(device)).to(torch.bfloat16)
     for n in range(needles):
         kv = n % hkv
-        pos = int(torch.randint(0, max(1, length - 128), (1,), generator=g))
-        row = int(torch.randint(pos + 1, length, (1,), generator=g)) if pos + 1 < length else pos
-        head = kv * group + int(torch.randint(0, group, (1,), generator=g))
-        bi = int(torch.randint(0, b, (1,), generator=g))
+        pos = int(rng.integers(0, max(1, length - 128)))
+        row = int(rng.integers(pos + 1, length)) if pos + 1 < length else pos
+        head = kv * group + int(rng.integers(0, group))
+        bi = int(rng.integers(0, b))
         k[bi, pos, kv] = (q[bi, row, head].float() * 4.0).to(torch.bfloat16)
     if apply_rope:
         q, k = rope(q), rope(k)

@@ -259,6 +259,21 @@ def test_config2_32k_properties_and_sampled_tiles():
     assert math.isfinite(a.float().abs().max().item())
 
 
+@pytest.mark.slow
+def test_config4_128k_sampled_tiles_and_properties():
+    """Config 4 (131072 tokens, 1024 blocks): late tiles route over eight 128-block chunks."""
+    q, k, v = synthetic.config_inputs("c4", seed=0)
+    run_fused_vs_oracle("mean_native", q, k, v, 0.08, [3, 600, 1023])
+    qd, kd, vd = cuda(q, k, v)
+    a = ops.prefill_attention(qd, kd, vd, "mean_native", 0.08, SCALE)
+    sel, idx, cnt = ops.export_routing("mean_native", 1, 131072, 28, 4)
+    assert int(cnt.sum()) == int(sel.sum()) <= 28 * 1024 * 1025 // 2
+    assert bool((idx.max(dim=2).values <= 1024).all())
+    b = ops.prefill_attention(qd, kd, vd, "mean_native", 0.08, SCALE)
+    assert torch.equal(a, b)
+    assert _capi.device_error() == 0
+
+
 def test_tcgen05_and_mma_exact_kernels_agree():
     shape = synthetic.LayerShape(1, 2048, 28, 4)
     q, k, v = cuda(*synthetic.attention_inputs(shape, seed=5, needles=3, structured_sigma=0.5))
@@ -276,12 +291,13 @@ def test_tcgen05_and_mma_exact_kernels_agree():
     assert _capi.device_error() == 0
 
 
-@pytest.mark.parametrize("length,heads,kv", [(2049, 14, 2), (32768, 28, 4), (40000, 10, 2)])
+@pytest.mark.parametrize("length,heads,kv", [(2049, 14, 2), (32768, 28, 4), (40000, 10, 2), (65600, 4, 2)])
 def test_tcgen05_and_mma_route_kernels_agree(length, heads, kv):
     """The tensor-core V1 routing (transposed products in TMEM, persistent CTAs) against the
     mma.sync kernel: scores within fp32 rounding, masks bit-exact outside the threshold band.
     40000 tokens give 313 blocks: items past 256 blocks stream their block means per unit, and
-    the last tile is ragged."""
+    the last tile is ragged. 65600 tokens give 513 blocks: heads of five chunks, more than a
+    warpgroup's two accumulator slots hold."""
     shape = synthetic.LayerShape(1, length, heads, kv)
     q, k, v = cuda(*synthetic.attention_inputs(shape, seed=length, needles=3, structured_sigma=0.5))
     mk = upstream.block_mean_k(k)
