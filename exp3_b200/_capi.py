@@ -145,6 +145,12 @@ def set_mean_kernel(name: str) -> None:
     call("fpx_set_option", 4, {"tcgen05": 0, "fp32": 1}[name])
 
 
+def set_selector_kernel(name: str) -> None:
+    """Selects the fused path's routing kernel for mean_balanced / cgf_mean / dispersion_mean:
+    "tcgen05" (the default) or "fp32" (the CUDA-core cross-check)."""
+    call("fpx_set_option", 5, {"tcgen05": 0, "fp32": 1}[name])
+
+
 def set_exp_emulation(pairs_of_8: int) -> None:
     """How many of every 8 exp2 pairs the tcgen05 kernel evaluates on the FMA pipe (0, 2, 3)."""
     call("fpx_set_option", 2, int(pairs_of_8))

@@ -26,11 +26,13 @@ int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int 
 
 // Process-wide options (fpx_set_option): which exact kernel the fused path runs, how many
 // of every 8 exp2 pairs the tcgen05 kernel computes on the FMA pipe (0, 2 or 3), which V1
-// routing kernel runs and which mean-tail kernel runs.
-enum Option { kOptExactKernel = 1, kOptExpEmulation = 2, kOptRouteKernel = 3, kOptMeanKernel = 4 };
+// routing kernel, mean-tail kernel and new-selector routing kernel run.
+enum Option { kOptExactKernel = 1, kOptExpEmulation = 2, kOptRouteKernel = 3, kOptMeanKernel = 4,
+              kOptSelectorKernel = 5 };
 enum ExactKernel { kExactKernelTcgen05 = 0, kExactKernelMmaSync = 1 };
 enum RouteKernel { kRouteKernelTcgen05 = 0, kRouteKernelMmaSync = 1 };
 enum MeanKernel { kMeanKernelTcgen05 = 0, kMeanKernelFp32 = 1 };
+enum SelectorKernel { kSelectorKernelTcgen05 = 0, kSelectorKernelFp32 = 1 };
 int get_option(int key);
 
 enum MeanMode { kMeanMergeInPlace = 0, kMeanStandalone = 1 };

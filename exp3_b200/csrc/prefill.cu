@@ -14,7 +14,7 @@ namespace fpx {
 struct Workspace {
   int32_t *lists, *counts;
   uint32_t *tail;
-  __nv_bfloat16 *mk16, *mkh, *mkl, *mvh;
+  __nv_bfloat16 *mk16, *mkh, *mkl, *mvh, *vkh, *vkl;
   float *mk, *mv, *vk, *sv, *lse;
   size_t bytes;
 };
@@ -38,6 +38,8 @@ static Workspace carve(void *base, int B, int L, int H, int Hkv) {
   w.mkh = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
   w.mkl = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
   w.mvh = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
+  w.vkh = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
+  w.vkl = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
   w.mk = reinterpret_cast<float *>(take(desc * 4));
   w.mv = reinterpret_cast<float *>(take(desc * 4));
   w.vk = reinterpret_cast<float *>(take(desc * 4));
@@ -75,15 +77,17 @@ extern "C" const char *fpx_status_string(int status) {
 extern "C" int fpx_version(void) { return 1; }
 
 namespace fpx {
-static int g_options[5] = {0, kExactKernelTcgen05, 0, kRouteKernelTcgen05, kMeanKernelTcgen05};
-int get_option(int key) { return (key > 0 && key < 5) ? g_options[key] : 0; }
+static int g_options[6] = {0, kExactKernelTcgen05, 0, kRouteKernelTcgen05, kMeanKernelTcgen05,
+                           kSelectorKernelTcgen05};
+int get_option(int key) { return (key > 0 && key < 6) ? g_options[key] : 0; }
 }  // namespace fpx
 
 extern "C" int fpx_set_option(int key, int value) {
   if ((key == kOptExactKernel && (value == kExactKernelTcgen05 || value == kExactKernelMmaSync)) ||
       (key == kOptExpEmulation && (value == 0 || value == 2 || value == 3)) ||
       (key == kOptRouteKernel && (value == kRouteKernelTcgen05 || value == kRouteKernelMmaSync)) ||
-      (key == kOptMeanKernel && (value == kMeanKernelTcgen05 || value == kMeanKernelFp32))) {
+      (key == kOptMeanKernel && (value == kMeanKernelTcgen05 || value == kMeanKernelFp32)) ||
+      (key == kOptSelectorKernel && (value == kSelectorKernelTcgen05 || value == kSelectorKernelFp32))) {
     g_options[key] = value;
     return FPX_OK;
   }
@@ -146,7 +150,7 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     st.L = L; st.nb = nb; st.Hkv = Hkv; st.kv_begin = kv_begin;
     st.mean_bf16 = ws.mk16; st.mean_k = ws.mk; st.mean_v = ws.mv; st.var_k = ws.vk;
     st.sigma_v = ws.sv; st.counts = nullptr;
-    st.mk_hi = ws.mkh; st.mk_lo = ws.mkl; st.mv_hi = ws.mvh;
+    st.mk_hi = ws.mkh; st.mk_lo = ws.mkl; st.mv_hi = ws.mvh; st.vk_hi = ws.vkh; st.vk_lo = ws.vkl;
     if (method == FPX_METHOD_DENSE) {
       rc = launch_causal_route(rv, H, head_begin, heads, tile_begin, tiles, B, s);
     } else if (method == FPX_METHOD_FP_V1 || method == FPX_METHOD_MEAN_NATIVE) {
@@ -172,7 +176,9 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
         sp.head_begin = head_begin; sp.tile_begin = tile_begin;
         sp.scale = (float)scale; sp.scale2 = (float)(scale * scale);
         sp.scores = nullptr; sp.sel = sel;
-        rc = launch_selector_route(sp, method, tiles, heads, B, s);
+        sp.mk_hi = ws.mkh; sp.mk_lo = ws.mkl; sp.vk_hi = ws.vkh; sp.vk_lo = ws.vkl;
+        rc = get_option(kOptSelectorKernel) == kSelectorKernelFp32 ? launch_selector_route(sp, method, tiles, heads, B, s)
+                                                                   : launch_selector_route_tc(sp, method, tiles, heads, B, s);
       }
     }
     if (rc) return rc;

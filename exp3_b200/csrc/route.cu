@@ -44,7 +44,13 @@ __global__ void __launch_bounds__(128) block_stats_kernel(StatsParams p) {
     const float mk = __fdiv_rn(sk, fn);
     const float mv = __fdiv_rn(sv, fn);
     p.mean_k[o] = mk;
-    p.var_k[o] = fmaxf(__fsub_rn(__fdiv_rn(sk2, fn), __fmul_rn(mk, mk)), 0.f);
+    const float vk = fmaxf(__fsub_rn(__fdiv_rn(sk2, fn), __fmul_rn(mk, mk)), 0.f);
+    p.var_k[o] = vk;
+    if (p.vk_hi) {
+      const __nv_bfloat16 hi = __float2bfloat16_rn(vk);
+      p.vk_hi[o] = hi;
+      p.vk_lo[o] = __float2bfloat16_rn(__fsub_rn(vk, __bfloat162float(hi)));
+    }
     p.mean_v[o] = mv;
     if (p.mk_hi) {  // mean_k = hi + lo exactly up to lo's rounding; the remainder is exact in fp32
       const __nv_bfloat16 hi = __float2bfloat16_rn(mk);

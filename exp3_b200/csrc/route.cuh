@@ -12,6 +12,7 @@ struct StatsParams {
   __nv_bfloat16 *mean_bf16;                      // [B][nb][Hkv][d] (V1 block mean)
   float *mean_k, *mean_v, *var_k, *sigma_v;      // fp32 descriptors
   __nv_bfloat16 *mk_hi, *mk_lo, *mv_hi;          // bf16 splits for the tensor-core tail, or null
+  __nv_bfloat16 *vk_hi, *vk_lo;                  // bf16 splits of var_k for the tensor-core selectors
   int32_t *counts;                               // [nb] or null
 };
 
@@ -37,6 +38,8 @@ struct SelParams {
   const __nv_bfloat16 *q;
   int64_t q_sb, q_sl, q_sh;
   const float *mean_k, *var_k, *sigma_v;
+  // bf16 high + low halves of mean_k and var_k for the tensor-core kernel (null for the fp32 one)
+  const __nv_bfloat16 *mk_hi, *mk_lo, *vk_hi, *vk_lo;
   int L, nb, H, Hkv, group, head_begin, tile_begin;
   float scale, scale2;          // fp32(scale), fp32(scale * scale)
   float *scores;
@@ -60,6 +63,8 @@ int launch_v1_route(const V1Params &p, int tiles, int heads, int B, cudaStream_t
 int launch_v1_route_tc(const V1Params &p, int B, int tiles, int heads, cudaStream_t s);
 // The kernel fpx_set_option(3, ...) selects.
 int launch_v1_route_selected(const V1Params &p, int tiles, int heads, int B, cudaStream_t s);
+// tcgen05 form (route_sel_tc.cu): needs the bf16 splits in p (the fused path's workspace).
+int launch_selector_route_tc(const SelParams &p, int selector, int tiles, int heads, int B, cudaStream_t s);
 int launch_selector_route(const SelParams &p, int selector, int tiles, int heads, int B,
                           cudaStream_t s);
 int launch_causal_route(const RouteView &r, int H, int head_begin, int heads, int tile_begin,

@@ -1,0 +1,413 @@
+// The new selectors' routing (kernels.py:49-126) on the 5th-generation tensor core, fused with
+// their selection (kernels.py:129-151).
+//
+// For query tile t of head h and every visible block kb < t (a full block, n = 128):
+//   ell0 = (q . mean_k) * scale + ln 128
+//   u    = max((q^2 . var_k) * scale^2, 0)        (cgf_mean, dispersion_mean)
+//   logit = ell0 (+ u / 2)
+//   p     = softmax over kb of the row's logits
+//   score = mean over the tile's rows of p (x sqrt(u) x sigma_v for dispersion_mean)
+//   keep  = score > 0 and score >= alpha * max score, plus the protected blocks.
+//
+// The products run on the tensor core in two passes over 128-block chunks:
+//   pass 1, row layout (TMEM lane = query row): S = Q . mean_K^T (and Q^2 . var_K^T); each
+//     thread keeps its row's running max and sum, giving the row's log-sum-exp;
+//   pass 2, transposed (TMEM lane = block): S^T = mean_K . Q^T (and var_K . (Q^2)^T); each
+//     thread owns one block and adds up its rows' probabilities (row LSEs from shared memory),
+//     so the column sums need no cross-thread reduction.
+// Precision: the fp32 descriptors enter as bf16 high + low halves (mean_k = hi + lo, lo the
+// rounding remainder), and Q^2 (exact in fp32: a bf16 square has 16 significant bits) splits
+// exactly into bf16 hi + lo; u accumulates Q2hi.VKhi + Q2lo.VKhi + Q2hi.VKlo. Logits carry about
+// 16 mantissa bits of the descriptors, against fp32's 24 in the reference.
+//
+// One CTA per (b, h, t); 256 threads:
+//   warp 0       TMA: Q, then the operand ring (chunk by chunk: mean-K hi, lo, var-K hi, lo)
+//   warp 1       MMA issuer (one lane), TMEM owner
+//   warps 2..3   square Q into Q2hi / Q2lo (same swizzled layout: squaring is elementwise)
+//   warps 4..7   epilogue: the two passes' reductions, then the selection
+// TMEM: two buffers x (logit accumulator, u accumulator) x 128 columns.
+// Waits are bounded; a failed wait flags the CTA and the device error word and the row is
+// written with count 0.
+#include <cuda.h>
+
+#include "route.cuh"
+#include "tc.cuh"
+
+namespace fpx {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kThreads = 256;
+constexpr int kMaxBlocks = 2048;
+constexpr uint32_t kHalf = 128 * 128;
+constexpr uint32_t kTile = 2 * kHalf;
+constexpr uint32_t kIdesc = idesc_bf16(128, 128, false);
+constexpr float kLn128 = 4.852030263919617f;
+
+struct alignas(1024) SelSmem {
+  uint8_t q[kTile], q2h[kTile], q2l[kTile];
+  uint8_t ring[2][kTile];
+  uint64_t q_full, q2_full, r_full[2], r_empty[2], acc_full[2], acc_empty[2], drain;
+  uint32_t tmem_base;
+  int abort;
+  float lse[128];
+  float red[2][8];
+  int scan[2][4 * (kMaxBlocks / 128)];
+  float sc[kMaxBlocks];
+};
+
+FPX_INLINE uint64_t desc_kmajor(const uint8_t *tile, int kk) {
+  return smem_desc_sw128(smem_u32(tile) + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+}
+
+// 8 MMAs: D (+)= A . B^T over K = 128, both K-major SW128 tiles.
+FPX_INLINE void mma_tile(uint32_t d, const uint8_t *a, const uint8_t *b, bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) mma_ss(d, desc_kmajor(a, kk), desc_kmajor(b, kk), kIdesc, (accumulate || kk > 0) ? 1u : 0u);
+}
+
+template <int kSel>
+FPX_INLINE float sel_logit(float dot, float udot, float scale, float scale2) {
+  const float ell0 = __fadd_rn(__fmul_rn(dot, scale), kLn128);
+  if (kSel == 0) return ell0;
+  const float u = fmaxf(__fmul_rn(udot, scale2), 0.f);
+  return __fadd_rn(ell0, 0.5f * u);
+}
+
+}  // namespace
+
+template <int kSel>  // 0 mean_balanced, 1 cgf_mean, 2 dispersion_mean
+__global__ void __launch_bounds__(kThreads, 1)
+    selector_route_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_mkh,
+                             const __grid_constant__ CUtensorMap tm_mkl, const __grid_constant__ CUtensorMap tm_vkh,
+                             const __grid_constant__ CUtensorMap tm_vkl, SelParams p, int *device_error) {
+  constexpr int kTilesPerChunk = kSel == 0 ? 2 : 4;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  SelSmem &sh = *reinterpret_cast<SelSmem *>(smem_raw + pad);
+  volatile int *abort = &sh.abort;
+  const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);
+  const int h = p.head_begin + blockIdx.y;
+  const int b = blockIdx.z;
+  const int kvh = h / p.group;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int chunks = (t + 127) / 128;  // visible blocks kb < t
+  const int units = 2 * chunks;        // pass 1 then pass 2, chunk by chunk
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sh.q_full, 1);
+    mbar_init(&sh.q2_full, 64);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sh.r_full[s], 1);
+      mbar_init(&sh.r_empty[s], 1);
+      mbar_init(&sh.acc_full[s], 1);
+      mbar_init(&sh.acc_empty[s], 128);
+    }
+    mbar_init(&sh.drain, 1);
+    sh.abort = *reinterpret_cast<volatile int *>(device_error) != 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sh.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    int n = 0;  // operand tiles issued
+    bool ok = !*abort && chunks > 0;
+    if (ok && lane == 0) {
+      mbar_expect_tx(&sh.q_full, kTile);
+      tma_load_4d(sh.q, &tm_q, &sh.q_full, 0, h, t * 128, b);
+      tma_load_4d(sh.q + kHalf, &tm_q, &sh.q_full, 64, h, t * 128, b);
+    }
+    for (int u = 0; u < units && ok; ++u) {
+      const int c = u % chunks;
+      for (int j = 0; j < kTilesPerChunk && ok; ++j, ++n) {
+        const int s = n & 1;
+        if (n >= 2 && !(ok = mbar_wait_warp(&sh.r_empty[s], ((n >> 1) - 1) & 1, abort))) break;
+        if (lane == 0) {
+          const CUtensorMap *map = j == 0 ? &tm_mkh : j == 1 ? &tm_mkl : j == 2 ? &tm_vkh : &tm_vkl;
+          mbar_expect_tx(&sh.r_full[s], kTile);
+          tma_load_4d(sh.ring[s], map, &sh.r_full[s], 0, kvh, c * 128, b);
+          tma_load_4d(sh.ring[s] + kHalf, map, &sh.r_full[s], 64, kvh, c * 128, b);
+        }
+      }
+    }
+    __syncwarp();
+    if (*abort && chunks > 0) {  // drain copies in flight before the shared memory goes away
+      int never = 0;
+      mbar_wait(&sh.q_full, 0, &never);
+      for (int s = 0; s < 2; ++s) {
+        const int issued = n / 2 + (s < (n & 1) ? 1 : 0);
+        if (issued > 0) mbar_wait(&sh.r_full[s], (issued - 1) & 1, &never);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    bool ok = !*abort && chunks > 0;
+    if (ok) ok = mbar_wait_warp(&sh.q_full, 0, abort);
+    if (ok && kSel > 0) ok = mbar_wait_warp(&sh.q2_full, 0, abort);
+    int n = 0;
+    for (int u = 0; u < units && ok; ++u) {
+      const bool transposed = u >= chunks;
+      const int a = u & 1;
+      if (u >= 2 && !(ok = mbar_wait_warp(&sh.acc_empty[a], ((u >> 1) - 1) & 1, abort))) break;
+      const uint32_t acc_l = tmem + 256 * a, acc_u = acc_l + 128;
+      for (int j = 0; j < kTilesPerChunk && ok; ++j, ++n) {
+        const int s = n & 1;
+        if (!(ok = mbar_wait_warp(&sh.r_full[s], (n >> 1) & 1, abort))) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint8_t *x = sh.ring[s];
+          if (!transposed) {  // rows x blocks
+            if (j < 2) {
+              mma_tile(acc_l, sh.q, x, j == 1);
+            } else if (j == 2) {
+              mma_tile(acc_u, sh.q2h, x, false);
+              mma_tile(acc_u, sh.q2l, x, true);
+            } else {
+              mma_tile(acc_u, sh.q2h, x, true);
+            }
+          } else {  // blocks x rows
+            if (j < 2) {
+              mma_tile(acc_l, x, sh.q, j == 1);
+            } else if (j == 2) {
+              mma_tile(acc_u, x, sh.q2h, false);
+              mma_tile(acc_u, x, sh.q2l, true);
+            } else {
+              mma_tile(acc_u, x, sh.q2h, true);
+            }
+          }
+          tc_commit(&sh.r_empty[s]);
+          if (j == kTilesPerChunk - 1) tc_commit(&sh.acc_full[a]);
+        }
+        __syncwarp();
+      }
+    }
+    if (*abort && chunks > 0) {
+      int never = 0;
+      if (lane == 0) tc_commit(&sh.drain);
+      __syncwarp();
+      mbar_wait(&sh.drain, 0, &never);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------------ Q^2 = hi + lo
+    if (kSel > 0 && chunks > 0) {
+      const bool ok = mbar_wait(&sh.q_full, 0, abort);
+      if (ok) {
+        const int tid = threadIdx.x - 64;
+        for (int i = tid; i < (int)(kTile / 16); i += 64) {
+          const uint4 v = reinterpret_cast<const uint4 *>(sh.q)[i];
+          const uint32_t *w = reinterpret_cast<const uint32_t *>(&v);
+          uint4 hi4, lo4;
+          uint32_t *hw = reinterpret_cast<uint32_t *>(&hi4), *lw = reinterpret_cast<uint32_t *>(&lo4);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[k]));
+            const float s0 = f.x * f.x, s1 = f.y * f.y;  // exact: 16 significant bits
+            const __nv_bfloat16 h0 = __float2bfloat16_rn(s0), h1 = __float2bfloat16_rn(s1);
+            const __nv_bfloat16 l0 = __float2bfloat16_rn(s0 - __bfloat162float(h0));
+            const __nv_bfloat16 l1 = __float2bfloat16_rn(s1 - __bfloat162float(h1));
+            hw[k] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+            lw[k] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+          }
+          reinterpret_cast<uint4 *>(sh.q2h)[i] = hi4;
+          reinterpret_cast<uint4 *>(sh.q2l)[i] = lo4;
+        }
+      }
+      fence_proxy_async();  // generic writes -> read by the tensor core
+      mbar_arrive(&sh.q2_full);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int ew = warp & 3;
+    const int e = ew * 32 + lane;                    // TMEM lane: row (pass 1) or block (pass 2)
+    const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
+    const int rows = min(kBlock, p.L - t * kBlock);  // valid query rows
+    const float scale = p.scale, scale2 = p.scale2;
+    bool ok = !*abort;
+    int red_k = 0;
+    auto grp_sync = [&]() { named_sync(1, 128); };
+    // Pass 1: row e's log-sum-exp over the visible blocks (log2 units).
+    float m = -INFINITY, ssum = 0.f;
+    for (int u = 0; u < chunks; ++u) {
+      const int a = u & 1;
+      if (ok) ok = mbar_wait_warp(&sh.acc_full[a], (u >> 1) & 1, abort);
+      tc_fence_after();
+      if (ok) {
+        const int ncol = min(128, t - 128 * u);  // visible columns of this chunk
+        float bmax = -INFINITY;
+        // max over the visible columns
+#pragma unroll 1
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float vl[32], vu[32];
+          tmem_ld32(tmem + lane_off + 256 * a + 32 * q4, vl);
+          if (kSel > 0) tmem_ld32(tmem + lane_off + 256 * a + 128 + 32 * q4, vu);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float l = sel_logit<kSel>(vl[c], kSel > 0 ? vu[c] : 0.f, scale, scale2) * kLog2e;
+            bmax = fmaxf(bmax, 32 * q4 + c < ncol ? l : -INFINITY);
+          }
+        }
+        const float mn = fmaxf(m, bmax);
+        float acc = (m == -INFINITY) ? 0.f : ssum * ex2(m - mn);
+#pragma unroll 1
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float vl[32], vu[32];
+          tmem_ld32(tmem + lane_off + 256 * a + 32 * q4, vl);
+          if (kSel > 0) tmem_ld32(tmem + lane_off + 256 * a + 128 + 32 * q4, vu);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float l = sel_logit<kSel>(vl[c], kSel > 0 ? vu[c] : 0.f, scale, scale2) * kLog2e;
+            acc += 32 * q4 + c < ncol ? ex2(l - mn) : 0.f;
+          }
+        }
+        m = mn;
+        ssum = acc;
+      }
+      tc_fence_before();
+      mbar_arrive(&sh.acc_empty[a]);
+    }
+    sh.lse[e] = m + __log2f(ssum);
+    grp_sync();
+    // Pass 2: block kb = 128 u' + e sums its rows' probabilities.
+    for (int u = chunks; u < 2 * chunks; ++u) {
+      const int a = u & 1, c = u - chunks;
+      if (ok) ok = mbar_wait_warp(&sh.acc_full[a], (u >> 1) & 1, abort);
+      tc_fence_after();
+      const int kb = 128 * c + e;
+      float colsum = 0.f;
+      if (ok && 128 * c + 32 * ew < t) {  // some block of this warp is visible
+#pragma unroll 1
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float vl[32], vu[32];
+          tmem_ld32(tmem + lane_off + 256 * a + 32 * q4, vl);
+          if (kSel > 0) tmem_ld32(tmem + lane_off + 256 * a + 128 + 32 * q4, vu);
+          tmem_wait_ld();
+#pragma unroll
+          for (int r = 0; r < 32; ++r) {
+            const int row = 32 * q4 + r;
+            const float l = sel_logit<kSel>(vl[r], kSel > 0 ? vu[r] : 0.f, scale, scale2) * kLog2e;
+            float w = ex2(l - sh.lse[row]);
+            if (kSel == 2) w *= sqrtf(fmaxf(__fmul_rn(vu[r], scale2), 0.f));
+            colsum += row < rows ? w : 0.f;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sh.acc_empty[a]);
+      if (kb < p.nb) {
+        float score = 0.f;
+        if (kb < t) {
+          if (kSel == 2) colsum *= p.sigma_v[((int64_t)b * p.nb + kb) * p.Hkv + kvh];
+          score = colsum / (float)rows;
+        }
+        sh.sc[kb] = score;
+      }
+    }
+    for (int kb = 128 * chunks + e; kb < p.nb; kb += 128) sh.sc[kb] = 0.f;
+    // Selection (kernels.py:129-151): keep = score > 0 and score >= alpha * max score, plus
+    // the protected blocks; the group agrees on success before anything is written.
+    float lx = 0.f;
+    for (int kb = e; kb < p.nb; kb += 128) lx = fmaxf(lx, sh.sc[kb]);
+    lx = warp_max(lx);
+    float *red = sh.red[red_k & 1];
+    if (lane == 0) {
+      red[ew] = lx;
+      red[4 + ew] = ok ? 1.f : 0.f;
+    }
+    grp_sync();
+    ++red_k;
+    const float smax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const bool wg_ok = (red[4] + red[5]) + (red[6] + red[7]) == 4.f;
+    if (p.scores && wg_ok)
+      for (int kb = e; kb < p.nb; kb += 128) p.scores[(((int64_t)b * p.nb + t) * p.nb + kb) * p.H + h] = sh.sc[kb];
+    const SelectArgs &sa = p.sel;
+    if (sa.route.lists) {
+      const float thr = smax * sa.alpha;
+      const int64_t rrow = sa.route.row(b, h, t, sa.H);
+      int32_t *list = sa.route.lists + rrow * sa.route.nb;
+      uint32_t *tail = sa.route.tail + rrow * sa.route.words;
+      auto active_at = [&](int kb) {
+        if (kb >= sa.nb || kb > t) return false;
+        const float s = sh.sc[kb];
+        return sa.all_causal || (s >= thr && s > 0.f) || is_protected(t, kb, sa.nb, sa.sink, sa.window, sa.last_full);
+      };
+      const int nch = (sa.nb + 127) / 128;
+      int *cnt = sh.scan[red_k & 1];
+      for (int j = 0; j < nch; ++j) {
+        const unsigned bal = __ballot_sync(0xffffffffu, active_at(128 * j + e));
+        if (lane == 0) cnt[4 * j + ew] = __popc(bal);
+      }
+      grp_sync();
+      ++red_k;
+      int base = 0;
+      for (int j = 0; j < nch; ++j) {
+        const int kb = 128 * j + e;
+        const bool active = active_at(kb);
+        const unsigned bal = __ballot_sync(0xffffffffu, active);
+        int pre = 0;
+        for (int w = 0; w < ew; ++w) pre += cnt[4 * j + w];
+        if (active && wg_ok) list[base + pre + __popc(bal & ((1u << lane) - 1u))] = kb;
+        const unsigned tb = __ballot_sync(0xffffffffu, kb < sa.nb && kb < t && !active);
+        if (lane == 0 && kb < sa.nb && wg_ok) tail[kb >> 5] = tb;
+        base += (cnt[4 * j] + cnt[4 * j + 1]) + (cnt[4 * j + 2] + cnt[4 * j + 3]);
+      }
+      if (e == 0) sa.route.counts[rrow] = wg_ok ? base : 0;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && sh.abort) atomicExch(device_error, 1);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+size_t selector_route_tc_smem() { return sizeof(SelSmem) + 1024; }
+
+int launch_selector_route_tc(const SelParams &p, int selector, int tiles, int heads, int B, cudaStream_t s) {
+  if (tiles <= 0 || heads <= 0) return FPX_OK;
+  if (p.nb > kMaxBlocks) return FPX_ERR_UNSUPPORTED;
+  if (!p.mk_hi || !p.mk_lo || !p.vk_hi || !p.vk_lo) return FPX_ERR_INVALID;
+  int *device_error = device_error_word();
+  if (!device_error) return FPX_ERR_CUDA;
+  const int64_t d = kHeadDim, dstride = (int64_t)p.Hkv * kHeadDim, bstride = (int64_t)p.nb * dstride;
+  CUtensorMap tq, tmkh, tmkl, tvkh, tvkl;
+  if (!encode_4d(&tq, p.q, d, p.H, p.L, B, p.q_sh, p.q_sl, p.q_sb) ||
+      !encode_4d(&tmkh, p.mk_hi, d, p.Hkv, p.nb, B, kHeadDim, dstride, bstride) ||
+      !encode_4d(&tmkl, p.mk_lo, d, p.Hkv, p.nb, B, kHeadDim, dstride, bstride) ||
+      !encode_4d(&tvkh, p.vk_hi, d, p.Hkv, p.nb, B, kHeadDim, dstride, bstride) ||
+      !encode_4d(&tvkl, p.vk_lo, d, p.Hkv, p.nb, B, kHeadDim, dstride, bstride))
+    return FPX_ERR_INVALID;
+  const dim3 grid(tiles, heads, B);
+  const size_t smem = selector_route_tc_smem();
+#define FPX_SEL_TC(K)                                                                                   \
+  do {                                                                                                  \
+    cudaFuncSetAttribute(selector_route_tc_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    selector_route_tc_kernel<K><<<grid, kThreads, smem, s>>>(tq, tmkh, tmkl, tvkh, tvkl, p, device_error); \
+  } while (0)
+  if (selector == FPX_METHOD_MEAN_BALANCED)
+    FPX_SEL_TC(0);
+  else if (selector == FPX_METHOD_CGF_MEAN)
+    FPX_SEL_TC(1);
+  else if (selector == FPX_METHOD_DISPERSION_MEAN)
+    FPX_SEL_TC(2);
+  else
+    return FPX_ERR_INVALID;
+#undef FPX_SEL_TC
+  FPX_CHECK_LAUNCH();
+  return FPX_OK;
+}
+
+}  // namespace fpx

@@ -71,7 +71,9 @@ int fpx_version(void);
  * selects the V1 routing kernel (fpx_prefill_attention and fpx_v1_scores): 0 = tcgen05,
  * transposed block-mean x Q products in TMEM (default), 1 = mma.sync (cross-check). Key 4
  * selects the mean-tail kernel of fpx_prefill_attention: 0 = tcgen05, block means as bf16
- * high + low halves (default), 1 = fp32 CUDA cores (cross-check). */
+ * high + low halves (default), 1 = fp32 CUDA cores (cross-check). Key 5 selects the
+ * routing kernel of the new selectors in fpx_prefill_attention: 0 = tcgen05, descriptors as
+ * bf16 high + low halves, two passes (default), 1 = fp32 CUDA cores (cross-check). */
 int fpx_set_option(int key, int value);
 
 /* Reads (and with reset != 0 clears) the device error word set when a bounded wait inside a

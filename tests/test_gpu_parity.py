@@ -339,6 +339,30 @@ def test_tcgen05_and_fp32_mean_tails_agree(length, heads, kv):
     assert _capi.device_error() == 0
 
 
+@pytest.mark.parametrize("method", ["mean_balanced", "cgf_mean", "dispersion_mean"])
+@pytest.mark.parametrize("length,heads,kv", [(4096, 14, 2), (40000, 10, 2)])
+def test_tcgen05_and_fp32_selector_routing_agree(method, length, heads, kv):
+    """The tensor-core selector routing (descriptors as bf16 high + low halves, two passes)
+    against the fp32 CUDA-core kernel: masks bit-exact outside the threshold band of the fp32
+    scores (fpx_selector_scores). 40000 tokens: late tiles span three 128-block chunks."""
+    shape = synthetic.LayerShape(1, length, heads, kv)
+    q, k, v = cuda(*synthetic.attention_inputs(shape, seed=length + 7, needles=3, structured_sigma=0.5))
+    sels = []
+    try:
+        for which in ("fp32", "tcgen05"):
+            _capi.set_selector_kernel(which)
+            ops.prefill_attention(q, k, v, method, 0.08, SCALE, stages=_capi.STAGE_ROUTE)
+            sels.append(ops.export_routing(method, 1, length, heads, kv)[0].cpu())
+    finally:
+        _capi.set_selector_kernel("tcgen05")
+    desc = kernels.block_descriptors(k, v)
+    scores = kernels.selector_scores(q, desc, SCALE, method).cpu()
+    blocks = oracle.num_blocks(length)
+    assert_masks_match(method, sels[1], sels[0], scores, 0.08, list(range(blocks)))
+    assert int(sels[1].sum()) < heads * blocks * (blocks + 1) // 2  # the structured inputs route blocks away
+    assert _capi.device_error() == 0
+
+
 @pytest.mark.slow
 def test_fused_prefill_divergent_head_lists_32k():
     """Two query heads of one KV group whose block lists differ a lot (structured routing at 32K):
