@@ -20,11 +20,12 @@
 // exactly into bf16 hi + lo; u accumulates Q2hi.VKhi + Q2lo.VKhi + Q2hi.VKlo. Logits carry about
 // 16 mantissa bits of the descriptors, against fp32's 24 in the reference.
 //
-// One CTA per (b, h, t); 256 threads:
+// One CTA per (b, h, t); 384 threads:
 //   warp 0       TMA: Q, then the operand ring (chunk by chunk: mean-K hi, lo, var-K hi, lo)
 //   warp 1       MMA issuer (one lane), TMEM owner
 //   warps 2..3   square Q into Q2hi / Q2lo (same swizzled layout: squaring is elementwise)
-//   warps 4..7   epilogue: the two passes' reductions, then the selection
+//   warps 4..11  epilogue, two warpgroups splitting each chunk's columns (pass 1) or rows
+//                (pass 2); then warpgroup 0 runs the selection
 // TMEM: two buffers x (logit accumulator, u accumulator) x 128 columns.
 // Waits are bounded; a failed wait flags the CTA and the device error word and the row is
 // written with count 0.
@@ -39,7 +40,7 @@ namespace {
 
 using namespace tc;
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
 constexpr int kMaxBlocks = 2048;
 constexpr uint32_t kHalf = 128 * 128;
 constexpr uint32_t kTile = 2 * kHalf;
@@ -53,6 +54,7 @@ struct alignas(1024) SelSmem {
   uint32_t tmem_base;
   int abort;
   float lse[128];
+  float part_m[2][128], part_s[2][128];  // the two warpgroups' halves
   float red[2][8];
   int scan[2][4 * (kMaxBlocks / 128)];
   float sc[kMaxBlocks];
@@ -103,7 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sh.r_full[s], 1);
       mbar_init(&sh.r_empty[s], 1);
       mbar_init(&sh.acc_full[s], 1);
-      mbar_init(&sh.acc_empty[s], 128);
+      mbar_init(&sh.acc_empty[s], 256);
     }
     mbar_init(&sh.drain, 1);
     sh.abort = *reinterpret_cast<volatile int *>(device_error) != 0;
@@ -227,6 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ epilogue
+    // Two warpgroups: in pass 1 group g reduces columns [64 g, 64 g + 64) of every chunk for
+    // its row, in pass 2 rows [64 g, 64 g + 64) for its block; the halves meet in shared memory.
+    const int g = (warp - 4) >> 2;
     const int ew = warp & 3;
     const int e = ew * 32 + lane;                    // TMEM lane: row (pass 1) or block (pass 2)
     const uint32_t lane_off = (uint32_t)(ew * 32) << 16;
@@ -234,86 +239,105 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale = p.scale, scale2 = p.scale2;
     bool ok = !*abort;
     int red_k = 0;
-    auto grp_sync = [&]() { named_sync(1, 128); };
-    // Pass 1: row e's log-sum-exp over the visible blocks (log2 units).
+    auto all_sync = [&]() { named_sync(1, 256); };
+    auto grp_sync = [&]() { named_sync(2, 128); };  // group 0 only (the selection)
+    // Pass 1: running max / sum of this half of row e (log2 units), 32 columns at a time.
     float m = -INFINITY, ssum = 0.f;
     for (int u = 0; u < chunks; ++u) {
       const int a = u & 1;
       if (ok) ok = mbar_wait_warp(&sh.acc_full[a], (u >> 1) & 1, abort);
       tc_fence_after();
-      if (ok) {
-        const int ncol = min(128, t - 128 * u);  // visible columns of this chunk
-        float bmax = -INFINITY;
-        // max over the visible columns
+      const int ncol = min(128, t - 128 * u);  // visible columns of this chunk
+      if (ok && 64 * g < ncol) {
 #pragma unroll 1
-        for (int q4 = 0; q4 < 4; ++q4) {
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int c0 = 64 * g + 32 * q2;
           float vl[32], vu[32];
-          tmem_ld32(tmem + lane_off + 256 * a + 32 * q4, vl);
-          if (kSel > 0) tmem_ld32(tmem + lane_off + 256 * a + 128 + 32 * q4, vu);
+          tmem_ld32(tmem + lane_off + 256 * a + c0, vl);
+          if (kSel > 0) tmem_ld32(tmem + lane_off + 256 * a + 128 + c0, vu);
           tmem_wait_ld();
+          float cmax = -INFINITY;
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
-            const float l = sel_logit<kSel>(vl[c], kSel > 0 ? vu[c] : 0.f, scale, scale2) * kLog2e;
-            bmax = fmaxf(bmax, 32 * q4 + c < ncol ? l : -INFINITY);
+            vl[c] = c0 + c < ncol ? sel_logit<kSel>(vl[c], kSel > 0 ? vu[c] : 0.f, scale, scale2) * kLog2e : -INFINITY;
+            cmax = fmaxf(cmax, vl[c]);
           }
-        }
-        const float mn = fmaxf(m, bmax);
-        float acc = (m == -INFINITY) ? 0.f : ssum * ex2(m - mn);
-#pragma unroll 1
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float vl[32], vu[32];
-          tmem_ld32(tmem + lane_off + 256 * a + 32 * q4, vl);
-          if (kSel > 0) tmem_ld32(tmem + lane_off + 256 * a + 128 + 32 * q4, vu);
-          tmem_wait_ld();
+          const float mn = fmaxf(m, cmax);
+          if (mn != -INFINITY) {
+            float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float l = sel_logit<kSel>(vl[c], kSel > 0 ? vu[c] : 0.f, scale, scale2) * kLog2e;
-            acc += 32 * q4 + c < ncol ? ex2(l - mn) : 0.f;
+            for (int c = 0; c < 32; c += 2) {
+              acc0 += ex2(vl[c] - mn);
+              acc1 += ex2(vl[c + 1] - mn);
+            }
+            ssum = (m == -INFINITY ? 0.f : ssum * ex2(m - mn)) + (acc0 + acc1);
+            m = mn;
           }
         }
-        m = mn;
-        ssum = acc;
       }
       tc_fence_before();
       mbar_arrive(&sh.acc_empty[a]);
     }
-    sh.lse[e] = m + __log2f(ssum);
-    grp_sync();
-    // Pass 2: block kb = 128 u' + e sums its rows' probabilities.
+    sh.part_m[g][e] = m;
+    sh.part_s[g][e] = ssum;
+    all_sync();
+    if (g == 0) {
+      const float m0 = sh.part_m[0][e], m1 = sh.part_m[1][e];
+      const float mm = fmaxf(m0, m1);
+      const float s0 = m0 == -INFINITY ? 0.f : sh.part_s[0][e] * ex2(m0 - mm);
+      const float s1 = m1 == -INFINITY ? 0.f : sh.part_s[1][e] * ex2(m1 - mm);
+      sh.lse[e] = mm + __log2f(s0 + s1);
+    }
+    all_sync();
+    // Pass 2: block kb = 128 c + e sums the probabilities of this group's rows.
     for (int u = chunks; u < 2 * chunks; ++u) {
       const int a = u & 1, c = u - chunks;
       if (ok) ok = mbar_wait_warp(&sh.acc_full[a], (u >> 1) & 1, abort);
       tc_fence_after();
       const int kb = 128 * c + e;
       float colsum = 0.f;
-      if (ok && 128 * c + 32 * ew < t) {  // some block of this warp is visible
+      if (ok && 128 * c + 32 * ew < t && 64 * g < rows) {  // some block of this warp is visible
 #pragma unroll 1
-        for (int q4 = 0; q4 < 4; ++q4) {
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int r0 = 64 * g + 32 * q2;
           float vl[32], vu[32];
-          tmem_ld32(tmem + lane_off + 256 * a + 32 * q4, vl);
-          if (kSel > 0) tmem_ld32(tmem + lane_off + 256 * a + 128 + 32 * q4, vu);
+          tmem_ld32(tmem + lane_off + 256 * a + r0, vl);
+          if (kSel > 0) tmem_ld32(tmem + lane_off + 256 * a + 128 + r0, vu);
           tmem_wait_ld();
+          float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
           for (int r = 0; r < 32; ++r) {
-            const int row = 32 * q4 + r;
+            const int row = r0 + r;
             const float l = sel_logit<kSel>(vl[r], kSel > 0 ? vu[r] : 0.f, scale, scale2) * kLog2e;
             float w = ex2(l - sh.lse[row]);
             if (kSel == 2) w *= sqrtf(fmaxf(__fmul_rn(vu[r], scale2), 0.f));
-            colsum += row < rows ? w : 0.f;
+            w = row < rows ? w : 0.f;
+            if (r & 1) acc1 += w; else acc0 += w;
           }
+          colsum += acc0 + acc1;
         }
       }
       tc_fence_before();
       mbar_arrive(&sh.acc_empty[a]);
-      if (kb < p.nb) {
+      if (g == 1) sh.part_s[1][e] = colsum;
+      all_sync();
+      if (g == 0 && kb < p.nb) {
         float score = 0.f;
         if (kb < t) {
-          if (kSel == 2) colsum *= p.sigma_v[((int64_t)b * p.nb + kb) * p.Hkv + kvh];
-          score = colsum / (float)rows;
+          float total = colsum + sh.part_s[1][e];
+          if (kSel == 2) total *= p.sigma_v[((int64_t)b * p.nb + kb) * p.Hkv + kvh];
+          score = total / (float)rows;
         }
         sh.sc[kb] = score;
       }
+      all_sync();
     }
+    if (g == 1) {  // the selection is group 0's; group 1 only reports whether its waits held
+      sh.part_m[1][e] = ok ? 1.f : 0.f;
+      all_sync();
+    } else {
+      all_sync();
+      ok = ok && sh.part_m[1][e] == 1.f;
     for (int kb = 128 * chunks + e; kb < p.nb; kb += 128) sh.sc[kb] = 0.f;
     // Selection (kernels.py:129-151): keep = score > 0 and score >= alpha * max score, plus
     // the protected blocks; the group agrees on success before anything is written.
@@ -363,6 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         base += (cnt[4 * j] + cnt[4 * j + 1]) + (cnt[4 * j + 2] + cnt[4 * j + 3]);
       }
       if (e == 0) sa.route.counts[rrow] = wg_ok ? base : 0;
+    }
     }
   }
   tc_fence_before();
