@@ -44,6 +44,9 @@ SIGNATURES = {
                              c_double, P, P, P], c_int),
     "fpx_mean_tail": ([P, *S3, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_double, P, P, P], c_int),
     "fpx_merge_exact_mean": ([P, P, P, P, c_i64, c_int, P, P, P], c_int),
+    "fpx_rescue_tail_workspace_bytes": ([c_int, c_int, c_int, c_int, c_int, c_int], c_size),
+    "fpx_rescue_tail": ([P, *S3, P, *S3, P, *S3, P, c_int, c_int, c_int, c_int, c_int, c_int, c_double, c_int,
+                         P, P, P, c_size, P], c_int),
     "fpx_prefill_workspace_bytes": ([c_int, c_int, c_int, c_int, c_int, c_int, c_int], c_size),
     "fpx_prefill_attention": ([c_int, c_double, c_int, c_int, c_int, P, *S3, P, *S3, P, *S3,
                                c_int, c_int, c_int, c_int, c_int, c_int, c_double,

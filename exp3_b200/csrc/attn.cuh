@@ -54,9 +54,17 @@ struct MeanParams {
   float *lse;
   // kMeanStandalone: fp32 mean-tail output [B][L][H][d] and LSE [B][L][H]
   float *mean_out, *mean_lse;
+  // rescue tails: K / V and the chosen token of every (b, h, t, kb), [B][H][nb][nb]
+  const __nv_bfloat16 *k, *v;
+  int64_t k_sb, k_sl, k_sh, v_sb, v_sl, v_sh;
+  uint8_t *choice;
 };
 
-int launch_mean_tail(const MeanParams &p, int mode, int tiles, int heads, int B, cudaStream_t s);
+// keys: 0 block means (mean_tail), 1 rescue tokens, 2 rescue tokens + remainder means.
+int launch_mean_tail(const MeanParams &p, int mode, int tiles, int heads, int B, cudaStream_t s, int keys = 0);
+// Rescue token of every tail block (kernels.py:276-285) into p.choice; the tail comes from the
+// route's bits (kMeanMergeInPlace) or from the mask (kMeanStandalone).
+int launch_rescue_choice(const MeanParams &p, int mode, int tiles, int kv_count, int B, cudaStream_t s);
 // tcgen05 / TMEM / TMA tail, merged in place (attn_tail_tc.cu); needs mk_hi, mk_lo, mv_hi.
 int launch_mean_tail_tc(const MeanParams &p, int B, int tiles, int heads, cudaStream_t s);
 int launch_merge(const __nv_bfloat16 *exact_out, const float *exact_lse, const float *mean_out,

@@ -9,14 +9,20 @@
 //
 // One CTA per (b, h, t) that has a tail; two threads per query row, each holding 64 of the
 // 128 dimensions (interleaved float4 chunks, so the pair reads distinct banks). The tail
-// blocks' descriptors are staged 16 at a time; the softmax runs online in fp32.
+// blocks' pseudo-keys are staged 16 at a time; the softmax runs online in fp32.
+//
+// The same kernel runs the rescue tails of fp_v1_rescue / _v2 (kernels.py:233-309, kKeys 1 / 2):
+// there the pseudo-key of tail block kb is its rescue token, the block's key row chosen by
+// rescue_choice_kernel (bf16 K / V, exact in fp32) with weight 1; _v2 adds the block's other
+// 127 tokens through their mean, K_rest = (sum K - k_rescue) / 127 (likewise V), with weight
+// ln 127. Tail blocks are full, so sum K = 128 x mean_k exactly (a power-of-two scale).
 #include "attn.cuh"
 
 namespace fpx {
 
 constexpr int kMeanChunk = 16;
 
-template <int kMode>
+template <int kMode, int kKeys>  // kKeys: 0 block means, 1 rescue tokens, 2 rescue + remainder
 __global__ void __launch_bounds__(256) mean_tail_kernel(MeanParams p) {
   const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);
   const int h = p.head_begin + blockIdx.y;
@@ -88,18 +94,47 @@ __global__ void __launch_bounds__(256) mean_tail_kernel(MeanParams p) {
   const float *mk_base = p.mean_k + ((int64_t)b * p.nb * p.Hkv + kvh) * kHeadDim;
   const float *mv_base = p.mean_v + ((int64_t)b * p.nb * p.Hkv + kvh) * kHeadDim;
 
-  for (int c0 = 0; c0 < ntail; c0 += kMeanChunk) {
-    const int cn = min(kMeanChunk, ntail - c0);
+  const int nkeys = kKeys == 2 ? 2 * ntail : ntail;  // pseudo-keys
+  const uint8_t *choice = kKeys ? p.choice + (((int64_t)b * p.H + h) * p.nb + t) * p.nb : nullptr;
+  for (int c0 = 0; c0 < nkeys; c0 += kMeanChunk) {
+    const int cn = min(kMeanChunk, nkeys - c0);
     __syncthreads();
     for (int i = tid; i < cn * 32; i += 256) {
       const int j = i >> 5, q4 = i & 31;
-      const int kb = list[c0 + j];
-      reinterpret_cast<float4 *>(smk + j * kHeadDim)[q4] =
-          reinterpret_cast<const float4 *>(mk_base + kb * dstride)[q4];
-      reinterpret_cast<float4 *>(smv + j * kHeadDim)[q4] =
-          reinterpret_cast<const float4 *>(mv_base + kb * dstride)[q4];
+      if (kKeys == 0) {
+        const int kb = list[c0 + j];
+        reinterpret_cast<float4 *>(smk + j * kHeadDim)[q4] =
+            reinterpret_cast<const float4 *>(mk_base + kb * dstride)[q4];
+        reinterpret_cast<float4 *>(smv + j * kHeadDim)[q4] =
+            reinterpret_cast<const float4 *>(mv_base + kb * dstride)[q4];
+      } else {
+        const int key = c0 + j;
+        const int kb = list[kKeys == 2 ? key >> 1 : key];
+        const int64_t tok = (int64_t)kb * kBlock + choice[kb];
+        const uint2 ku = *reinterpret_cast<const uint2 *>(p.k + b * p.k_sb + tok * p.k_sl + kvh * p.k_sh + 4 * q4);
+        const uint2 vu = *reinterpret_cast<const uint2 *>(p.v + b * p.v_sb + tok * p.v_sl + kvh * p.v_sh + 4 * q4);
+        const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&ku.x));
+        const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&ku.y));
+        const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vu.x));
+        const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vu.y));
+        float4 k4 = make_float4(k01.x, k01.y, k23.x, k23.y), v4 = make_float4(v01.x, v01.y, v23.x, v23.y);
+        if (kKeys == 2 && (key & 1)) {  // the block's other tokens: (sum - rescue) / 127
+          const float4 mk4 = reinterpret_cast<const float4 *>(mk_base + kb * dstride)[q4];
+          const float4 mv4 = reinterpret_cast<const float4 *>(mv_base + kb * dstride)[q4];
+          auto rest = [](float mean, float x) { return __fdiv_rn(__fsub_rn(__fmul_rn(mean, 128.f), x), 127.f); };
+          k4 = make_float4(rest(mk4.x, k4.x), rest(mk4.y, k4.y), rest(mk4.z, k4.z), rest(mk4.w, k4.w));
+          v4 = make_float4(rest(mv4.x, v4.x), rest(mv4.y, v4.y), rest(mv4.z, v4.z), rest(mv4.w, v4.w));
+        }
+        reinterpret_cast<float4 *>(smk + j * kHeadDim)[q4] = k4;
+        reinterpret_cast<float4 *>(smv + j * kHeadDim)[q4] = v4;
+      }
     }
-    if (tid < cn) slogn[tid] = logf((float)min(kBlock, p.L - list[c0 + tid] * kBlock));
+    if (tid < cn) {
+      if (kKeys == 0)
+        slogn[tid] = logf((float)min(kBlock, p.L - list[c0 + tid] * kBlock));
+      else
+        slogn[tid] = (kKeys == 2 && ((c0 + tid) & 1)) ? logf((float)(kBlock - 1)) : 0.f;
+    }
     __syncthreads();
     for (int j = 0; j < cn; ++j) {
       const float4 *mk4 = reinterpret_cast<const float4 *>(smk + j * kHeadDim);
@@ -166,19 +201,29 @@ __global__ void __launch_bounds__(256) mean_tail_kernel(MeanParams p) {
   }
 }
 
-int launch_mean_tail(const MeanParams &p, int mode, int tiles, int heads, int B, cudaStream_t s) {
+namespace {
+template <int kMode, int kKeys>
+void launch_tail_variant(const MeanParams &p, dim3 grid, size_t smem, cudaStream_t s) {
+  cudaFuncSetAttribute(mean_tail_kernel<kMode, kKeys>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  mean_tail_kernel<kMode, kKeys><<<grid, 256, smem, s>>>(p);
+}
+}  // namespace
+
+int launch_mean_tail(const MeanParams &p, int mode, int tiles, int heads, int B, cudaStream_t s, int keys) {
   if (tiles <= 0 || heads <= 0) return FPX_OK;
   const size_t smem = (size_t)2 * kMeanChunk * kHeadDim * 4 + kMeanChunk * 4 + 32 + (size_t)p.nb * 4;
   if (smem > 200 * 1024) return FPX_ERR_UNSUPPORTED;
+  if (keys != 0 && (!p.choice || !p.k || !p.v)) return FPX_ERR_INVALID;
   dim3 grid(tiles, heads, B);
-  if (mode == kMeanMergeInPlace) {
-    cudaFuncSetAttribute(mean_tail_kernel<kMeanMergeInPlace>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    mean_tail_kernel<kMeanMergeInPlace><<<grid, 256, smem, s>>>(p);
-  } else {
-    cudaFuncSetAttribute(mean_tail_kernel<kMeanStandalone>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    mean_tail_kernel<kMeanStandalone><<<grid, 256, smem, s>>>(p);
+  const bool merge = mode == kMeanMergeInPlace;
+  switch (keys) {
+    case 0: merge ? launch_tail_variant<kMeanMergeInPlace, 0>(p, grid, smem, s)
+                  : launch_tail_variant<kMeanStandalone, 0>(p, grid, smem, s); break;
+    case 1: merge ? launch_tail_variant<kMeanMergeInPlace, 1>(p, grid, smem, s)
+                  : launch_tail_variant<kMeanStandalone, 1>(p, grid, smem, s); break;
+    case 2: merge ? launch_tail_variant<kMeanMergeInPlace, 2>(p, grid, smem, s)
+                  : launch_tail_variant<kMeanStandalone, 2>(p, grid, smem, s); break;
+    default: return FPX_ERR_INVALID;
   }
   FPX_CHECK_LAUNCH();
   return FPX_OK;

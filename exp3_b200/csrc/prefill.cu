@@ -15,6 +15,7 @@ struct Workspace {
   int32_t *lists, *counts;
   uint32_t *tail;
   __nv_bfloat16 *mk16, *mkh, *mkl, *mvh, *vkh, *vkl;
+  uint8_t *choice;  // rescue token of every (b, h, t, kb), [B][H][nb][nb]
   float *mk, *mv, *vk, *sv, *lse;
   size_t bytes;
 };
@@ -45,12 +46,17 @@ static Workspace carve(void *base, int B, int L, int H, int Hkv) {
   w.vk = reinterpret_cast<float *>(take(desc * 4));
   w.sv = reinterpret_cast<float *>(take((size_t)B * nb * Hkv * 4));
   w.lse = reinterpret_cast<float *>(take((size_t)B * L * H * 4));
+  w.choice = static_cast<uint8_t *>(take((size_t)B * H * nb * nb));
   w.bytes = off;
   return w;
 }
 
 static bool aligned16(const void *p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 static bool strides_ok(int64_t a, int64_t b, int64_t c) { return a % 8 == 0 && b % 8 == 0 && c % 8 == 0; }
+
+static bool is_rescue_method(int m) {
+  return m == FPX_METHOD_FP_V1_RESCUE || m == FPX_METHOD_FP_V1_RESCUE_V2;
+}
 
 static bool is_mean_method(int m) {
   return m == FPX_METHOD_MEAN_NATIVE || m == FPX_METHOD_MEAN_BALANCED || m == FPX_METHOD_CGF_MEAN ||
@@ -112,8 +118,6 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
                                      int stages, fpx_stream_t stream) {
   FPX_BIND(stream);
   if (method < 0 || method > FPX_METHOD_FP_V1_RESCUE_V2) return FPX_ERR_INVALID;
-  if (method == FPX_METHOD_FP_V1_RESCUE || method == FPX_METHOD_FP_V1_RESCUE_V2)
-    return FPX_ERR_UNSUPPORTED;
   if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
   if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
       !aligned16(out))
@@ -153,8 +157,9 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     st.mk_hi = ws.mkh; st.mk_lo = ws.mkl; st.mv_hi = ws.mvh; st.vk_hi = ws.vkh; st.vk_lo = ws.vkl;
     if (method == FPX_METHOD_DENSE) {
       rc = launch_causal_route(rv, H, head_begin, heads, tile_begin, tiles, B, s);
-    } else if (method == FPX_METHOD_FP_V1 || method == FPX_METHOD_MEAN_NATIVE) {
-      rc = launch_block_stats(st, tile_end, kv_count, B, true, method == FPX_METHOD_MEAN_NATIVE, s);
+    } else if (method == FPX_METHOD_FP_V1 || method == FPX_METHOD_MEAN_NATIVE || is_rescue_method(method)) {
+      // V1 routing (attention.py:25); mean_native and the rescue tails also use the fp32 means
+      rc = launch_block_stats(st, tile_end, kv_count, B, true, method != FPX_METHOD_FP_V1, s);
       if (rc) return rc;
       V1Params vp{};
       vp.q = qb; vp.q_sb = q_sb; vp.q_sl = q_sl; vp.q_sh = q_sh;
@@ -211,6 +216,23 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     mp.lse = lse_out;
     rc = get_option(kOptMeanKernel) == kMeanKernelFp32 ? launch_mean_tail(mp, kMeanMergeInPlace, tiles, heads, B, s)
                                                        : launch_mean_tail_tc(mp, B, tiles, heads, s);
+  }
+  if ((stages & FPX_STAGE_MEAN) && is_rescue_method(method)) {
+    // attention.py:306-331: rescue tail (kernels.py:233-309), merged in place like the mean tail
+    MeanParams mp{};
+    mp.q = qb; mp.q_sb = q_sb; mp.q_sl = q_sl; mp.q_sh = q_sh;
+    mp.k = kb; mp.k_sb = k_sb; mp.k_sl = k_sl; mp.k_sh = k_sh;
+    mp.v = vb; mp.v_sb = v_sb; mp.v_sl = v_sl; mp.v_sh = v_sh;
+    mp.mean_k = ws.mk; mp.mean_v = ws.mv; mp.choice = ws.choice;
+    mp.L = L; mp.nb = nb; mp.H = H; mp.Hkv = Hkv; mp.group = G;
+    mp.head_begin = head_begin; mp.tile_begin = tile_begin;
+    mp.scale = (float)scale; mp.route = rv;
+    mp.out = static_cast<__nv_bfloat16 *>(out); mp.o_sb = o_sb; mp.o_sl = o_sl; mp.o_sh = o_sh;
+    mp.lse = lse_out;
+    rc = launch_rescue_choice(mp, kMeanMergeInPlace, tiles, kv_count, B, s);
+    if (rc) return rc;
+    rc = launch_mean_tail(mp, kMeanMergeInPlace, tiles, heads, B, s,
+                          method == FPX_METHOD_FP_V1_RESCUE_V2 ? 2 : 1);
   }
   return rc;
 }
@@ -283,6 +305,74 @@ extern "C" int fpx_mean_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_t 
   mp.head_begin = 0; mp.tile_begin = 0; mp.scale = (float)scale;
   mp.mask = selected; mp.mean_out = out; mp.mean_lse = lse;
   return launch_mean_tail(mp, kMeanStandalone, mp.nb, H, B, stream);
+}
+
+namespace fpx {
+struct RescueWorkspace {
+  uint8_t *choice;
+  float *mk, *mv, *vk, *sv;
+  size_t bytes;
+};
+static RescueWorkspace carve_rescue(void *base, int B, int L, int H, int Hkv) {
+  const int64_t nb = (L + kBlock - 1) / kBlock;
+  const size_t desc = (size_t)B * nb * Hkv * kHeadDim;
+  RescueWorkspace w{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t *p = base ? static_cast<uint8_t *>(base) + off : nullptr;
+    off += align256(bytes);
+    return p;
+  };
+  w.choice = take((size_t)B * H * nb * nb);
+  w.mk = reinterpret_cast<float *>(take(desc * 4));
+  w.mv = reinterpret_cast<float *>(take(desc * 4));
+  w.vk = reinterpret_cast<float *>(take(desc * 4));
+  w.sv = reinterpret_cast<float *>(take((size_t)B * nb * Hkv * 4));
+  w.bytes = off;
+  return w;
+}
+}  // namespace fpx
+
+extern "C" size_t fpx_rescue_tail_workspace_bytes(int B, int L, int H, int Hkv, int d, int block) {
+  if (d != kHeadDim || block != kBlock || B <= 0 || L <= 0 || H <= 0 || Hkv <= 0) return 0;
+  return carve_rescue(nullptr, B, L, H, Hkv).bytes;
+}
+
+extern "C" int fpx_rescue_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                               const void *k, int64_t k_sb, int64_t k_sl, int64_t k_sh,
+                               const void *v, int64_t v_sb, int64_t v_sl, int64_t v_sh,
+                               const uint8_t *selected, int B, int L, int H, int Hkv, int d, int block,
+                               double scale, int remainder, float *out, float *lse, void *workspace,
+                               size_t workspace_bytes, fpx_stream_t stream) {
+  FPX_BIND(stream);
+  if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
+  if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
+      !selected || !aligned16(out) || !lse)
+    return FPX_ERR_INVALID;
+  if (H % Hkv || !strides_ok(q_sb, q_sl, q_sh) || !strides_ok(k_sb, k_sl, k_sh) || !strides_ok(v_sb, v_sl, v_sh))
+    return FPX_ERR_SHAPE;
+  const RescueWorkspace ws = carve_rescue(workspace, B, L, H, Hkv);
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) || workspace_bytes < ws.bytes)
+    return FPX_ERR_WORKSPACE;
+  const int nb = (L + kBlock - 1) / kBlock;
+  StatsParams st{};
+  st.k = static_cast<const __nv_bfloat16 *>(k); st.k_sb = k_sb; st.k_sl = k_sl; st.k_sh = k_sh;
+  st.v = static_cast<const __nv_bfloat16 *>(v); st.v_sb = v_sb; st.v_sl = v_sl; st.v_sh = v_sh;
+  st.L = L; st.nb = nb; st.Hkv = Hkv; st.kv_begin = 0;
+  st.mean_k = ws.mk; st.mean_v = ws.mv; st.var_k = ws.vk; st.sigma_v = ws.sv;
+  int rc = launch_block_stats(st, nb, Hkv, B, false, true, stream);
+  if (rc) return rc;
+  MeanParams mp{};
+  mp.q = static_cast<const __nv_bfloat16 *>(q); mp.q_sb = q_sb; mp.q_sl = q_sl; mp.q_sh = q_sh;
+  mp.k = st.k; mp.k_sb = k_sb; mp.k_sl = k_sl; mp.k_sh = k_sh;
+  mp.v = st.v; mp.v_sb = v_sb; mp.v_sl = v_sl; mp.v_sh = v_sh;
+  mp.mean_k = ws.mk; mp.mean_v = ws.mv; mp.choice = ws.choice;
+  mp.L = L; mp.nb = nb; mp.H = H; mp.Hkv = Hkv; mp.group = H / Hkv;
+  mp.head_begin = 0; mp.tile_begin = 0; mp.scale = (float)scale;
+  mp.mask = selected; mp.mean_out = out; mp.mean_lse = lse;
+  rc = launch_rescue_choice(mp, kMeanStandalone, nb, Hkv, B, stream);
+  if (rc) return rc;
+  return launch_mean_tail(mp, kMeanStandalone, nb, H, B, stream, remainder ? 2 : 1);
 }
 
 extern "C" int fpx_merge_exact_mean(const void *exact_out, const float *exact_lse,

@@ -13,7 +13,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ._capi import METHOD_IDS, call, ptr, require_cuda, stream, strides3
+from ._capi import METHOD_IDS, call, lib, ptr, require_cuda, stream, strides3
 
 BLOCK_SIZE = 128
 SELECTORS = ("mean_balanced", "cgf_mean", "dispersion_mean")
@@ -119,9 +119,25 @@ def mean_tail(q, descriptors: BlockDescriptors, selected, scale: float, block_si
     return out, lse
 
 
+@torch.no_grad()
 def rescue_tail(q, k, v, selected, scale, block_size=BLOCK_SIZE, chunk_tiles=8, remainder=False):
-    """``kernels.py:233-309`` (fp_v1_rescue / _v2) is not built in this library."""
-    raise NotImplementedError("rescue_tail (fp_v1_rescue, fp_v1_rescue_v2) is not built in libfpx")
+    """``kernels.py:233-309``: exact attention to one rescue token per unselected full-history
+    block (the key maximising the tile's mean query . k), with ``remainder`` also the block's
+    other tokens through their mean with weight B - 1. Returns (fp32 O, fp32 natural LSE) over
+    these entries only, for ``merge_exact_mean``. ``chunk_tiles`` only batches the reference's
+    torch work and does not change the result."""
+    dev = require_cuda(q, k, v, selected)
+    batch, sequence, heads, head_dim = q.shape
+    kv_heads = k.shape[2]
+    out = torch.empty(batch, sequence, heads, head_dim, dtype=torch.float32, device=dev)
+    lse = torch.empty(batch, sequence, heads, dtype=torch.float32, device=dev)
+    nbytes = lib().fpx_rescue_tail_workspace_bytes(batch, sequence, heads, kv_heads, head_dim, block_size)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+    selected = selected.to(torch.bool).contiguous()
+    call("fpx_rescue_tail", ptr(q), *strides3(q), ptr(k), *strides3(k), ptr(v), *strides3(v), ptr(selected),
+         batch, sequence, heads, kv_heads, head_dim, block_size, float(scale), 1 if remainder else 0,
+         ptr(out), ptr(lse), ptr(ws), ws.numel(), stream(dev))
+    return out, lse
 
 
 @torch.no_grad()

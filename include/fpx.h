@@ -49,8 +49,8 @@ enum fpx_method {
   FPX_METHOD_MEAN_BALANCED = 3,
   FPX_METHOD_CGF_MEAN = 4,
   FPX_METHOD_DISPERSION_MEAN = 5,
-  FPX_METHOD_FP_V1_RESCUE = 6,   /* not built: returns FPX_ERR_UNSUPPORTED */
-  FPX_METHOD_FP_V1_RESCUE_V2 = 7 /* not built: returns FPX_ERR_UNSUPPORTED */
+  FPX_METHOD_FP_V1_RESCUE = 6,   /* V1 routing + exact + rescue-token tail (kernels.py:233-309) */
+  FPX_METHOD_FP_V1_RESCUE_V2 = 7 /* the same, plus the remainder means (remainder=True) */
 };
 
 /* Stage bits for fpx_prefill_attention (the profile stages of attention.py:66-75). */
@@ -150,6 +150,19 @@ int fpx_mean_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
                   const float *mean_k, const float *mean_v, const int32_t *counts,
                   const uint8_t *selected, int B, int L, int H, int Hkv, int d, int block,
                   double scale, float *out, float *lse, fpx_stream_t stream);
+
+/* kernels.py:233-309 rescue_tail: for every unselected full-history block of each (query tile,
+ * head), exact attention to its rescue token (the key maximising the tile's mean query . k,
+ * ties to the first), and with remainder != 0 also to the block's other 127 tokens through
+ * their mean with weight ln 127 -> out fp32 [B, L, H, d], lse fp32 [B, L, H] (-inf without
+ * tail). selected is the [B, nb, nb, H] bool mask. The workspace (fpx_rescue_tail_workspace_bytes,
+ * 256-byte aligned) holds the choices and the block means; reused across calls. */
+size_t fpx_rescue_tail_workspace_bytes(int B, int L, int H, int Hkv, int d, int block);
+int fpx_rescue_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh, const void *k, int64_t k_sb,
+                    int64_t k_sl, int64_t k_sh, const void *v, int64_t v_sb, int64_t v_sl, int64_t v_sh,
+                    const uint8_t *selected, int B, int L, int H, int Hkv, int d, int block, double scale,
+                    int remainder, float *out, float *lse, void *workspace, size_t workspace_bytes,
+                    fpx_stream_t stream);
 
 /* kernels.py:312-325 merge_exact_mean over rows = B * L * H rows of d: out (bf16, the
  * exact output's dtype) and lse fp32. */

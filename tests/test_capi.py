@@ -56,7 +56,12 @@ def test_argument_errors_are_statuses_not_crashes():
     assert rc == -3  # head_dim 64 is not compiled
     rc = lib.fpx_prefill_attention(6, 0.08, 2, 4, 2, *([None, 0, 0, 0] * 3), 1, 128, 28, 4, 128, 128,
                                    0.088, 0, 4, 0, 1, None, 0, 0, 0, None, None, 0, 7, None)
-    assert rc == -3  # the rescue methods are not built
+    assert rc == -1  # null tensors
+    rc = lib.fpx_prefill_attention(8, 0.08, 2, 4, 2, *([None, 0, 0, 0] * 3), 1, 128, 28, 4, 128, 128,
+                                   0.088, 0, 4, 0, 1, None, 0, 0, 0, None, None, 0, 7, None)
+    assert rc == -1  # no method 8
+    assert lib.fpx_rescue_tail_workspace_bytes(1, 1153, 4, 2, 128, 128) >= 4 * 10 * 10
+    assert lib.fpx_rescue_tail_workspace_bytes(1, 1153, 4, 2, 64, 128) == 0
 
 
 def test_ops_refuse_cpu_tensors():

@@ -106,6 +106,16 @@ def test_exact_mean_and_merge_match_reference():
         assert int(acc[key]) == int(ref[key]), key
 
 
+def test_rescue_tails_match_reference():
+    data, q, k, v = load("rescue_l1153.npz")
+    selected = t(data["selected"])
+    rows = t(data["rows"])
+    for name, remainder in (("rescue", False), ("rescue_v2", True)):
+        out, lse = kernels.rescue_tail(*cuda(q, k, v, selected), SCALE, remainder=remainder)
+        torch.testing.assert_close(lse.cpu(), t(data[f"{name}_lse"]), atol=LSE_TOL, rtol=0)
+        torch.testing.assert_close(out.cpu()[:, rows], t(data[f"{name}_out_rows"]), atol=O_TOL, rtol=0)
+
+
 # --------------------------------------------------------------------------- fused path vs oracle
 
 
@@ -142,7 +152,7 @@ def run_fused_vs_oracle(method, q, k, v, alpha, tiles):
 
 
 @pytest.mark.parametrize("method", ["dense", "fp_v1", "mean_native", "mean_balanced", "cgf_mean",
-                                    "dispersion_mean"])
+                                    "dispersion_mean", "fp_v1_rescue", "fp_v1_rescue_v2"])
 def test_fused_prefill_small(method):
     shape = synthetic.LayerShape(1, 2049, 14, 2)
     q, k, v = synthetic.attention_inputs(shape, seed=31, needles=4, structured_sigma=0.5)
