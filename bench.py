@@ -297,13 +297,20 @@ def run_model(args, rank, world, local):
         prefill_ms = timed(lambda: model.prefill(ids, args.decode_tokens), args.steps)
     first = model.prefill(ids, args.decode_tokens)
 
-    def decode_all():
+    def decode_eager():
         model.length = args.prompt_length
         tok = first
         for _ in range(args.decode_tokens - 1):
             tok = model.decode_step(tok)
 
-    decode_ms = timed(decode_all, 1) / max(1, args.decode_tokens - 1)
+    def decode_graph():
+        model.length = args.prompt_length
+        model.decode_graph(first, args.decode_tokens)
+
+    # Per token over the decode_tokens - 1 steps after the prefill's token (evaluate.py:384-400);
+    # the graph run includes its one eager warm-up step and the capture.
+    decode_eager_ms = timed(decode_eager, 1) / max(1, args.decode_tokens - 1)
+    decode_ms = timed(decode_graph, 1) / max(1, args.decode_tokens - 1)
     # End to end (evaluate.prefill): token ids from pinned host memory, prefill, first token to host.
     result = torch.empty(1, dtype=torch.int64).pin_memory()
 
@@ -323,7 +330,8 @@ def run_model(args, rank, world, local):
                            "method": args.method, "alpha": args.alpha,
                            "parallelism": f"tp{world} (heads / FFN sharded, NCCL all-reduce after o_proj and down)",
                            "prefill_tflops_dense_equivalent": flops / (prefill_ms * 1e-3) / 1e12,
-                           "decode_ms_per_token": decode_ms, "decode_tokens": args.decode_tokens},
+                           "decode_ms_per_token": decode_ms, "decode_ms_per_token_eager": decode_eager_ms,
+                           "decode": "CUDA-graph steps (Model.decode_graph)", "decode_tokens": args.decode_tokens},
                 "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": ids_host.numel() * 8,
                         "d2h_bytes_per_step": 8},
                 "clocks": clocks.summary()}

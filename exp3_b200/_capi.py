@@ -54,10 +54,13 @@ SIGNATURES = {
     "fpx_decode_workspace_bytes": ([c_int, c_int, c_int, c_int, c_int, c_int], c_size),
     "fpx_decode_attention": ([P, *S3, P, *S3, P, *S3, c_int, c_int, c_int, c_int, c_int, c_int, c_double,
                               P, *S3, P, P, c_size, P], c_int),
+    "fpx_decode_attention_at": ([P, *S3, P, *S3, P, *S3, c_int, c_int, c_int, P, c_int, c_int, c_int, c_double,
+                                 P, *S3, P, P, c_size, P], c_int),
     "fpx_decode_attention_noalloc": ([P, *S3, P, *S3, P, *S3, c_int, c_int, c_int, c_int, c_int, c_int,
                                       c_double, P, *S3, P, P], c_int),
     "fpx_rmsnorm": ([P, P, P, c_double, c_i64, c_int, P, P, P], c_int),
     "fpx_rope_neox": ([P, *S3, c_int, c_int, c_int, c_int, c_int, c_double, P], c_int),
+    "fpx_rope_neox_at": ([P, *S3, c_int, c_int, c_int, c_int, P, c_double, P], c_int),
     "fpx_silu_mul": ([P, c_i64, c_int, P, P], c_int),
     "fpx_prefill_export_routing": ([c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, c_size, P, P, P, P],
                                    c_int),

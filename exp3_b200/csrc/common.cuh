@@ -149,6 +149,10 @@ FPX_INLINE float logaddexp(float a, float b) {
 // stream current before launching, so multi-GPU callers need no extra set-up.
 static inline int fpx_bind_stream_device(cudaStream_t s) {
   if (!s) return FPX_OK;
+  // While a stream is being captured into a CUDA graph, device queries on it are not allowed
+  // (they would invalidate the capture); the capturing thread is already on the stream's device.
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &capture) == cudaSuccess && capture != cudaStreamCaptureStatusNone) return FPX_OK;
   int dev = -1, cur = -1;
   if (cudaStreamGetDevice(s, &dev) != cudaSuccess) return FPX_ERR_INVALID;
   if (cudaGetDevice(&cur) != cudaSuccess || cur != dev) {

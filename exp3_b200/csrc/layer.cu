@@ -63,6 +63,7 @@ struct RopeParams {
   int64_t n;  // B * L * heads * 64 threads of work
   int L, heads;
   int pos0;
+  const int32_t *pos_dev;  // if set, the position of row 0 is read here (CUDA-graph replays)
   float inv_freq[64];
 };
 
@@ -76,7 +77,7 @@ __global__ void __launch_bounds__(256) rope_kernel(RopeParams p) {
   const int64_t bl = rest / p.heads;
   const int l = (int)(bl % p.L);
   const int b = (int)(bl / p.L);
-  const float ang = (float)(p.pos0 + l) * p.inv_freq[i];
+  const float ang = (float)((p.pos_dev ? *p.pos_dev : p.pos0) + l) * p.inv_freq[i];
   const float c = __bfloat162float(__float2bfloat16_rn(cosf(ang)));
   const float s = __bfloat162float(__float2bfloat16_rn(sinf(ang)));
   __nv_bfloat16 *v = p.x + b * p.sb + (int64_t)l * p.sl + (int64_t)h * p.sh;
@@ -128,14 +129,13 @@ extern "C" int fpx_rmsnorm(const void *x, const void *residual, const void *weig
   return FPX_OK;
 }
 
-extern "C" int fpx_rope_neox(void *x, int64_t x_sb, int64_t x_sl, int64_t x_sh, int B, int L, int heads, int d,
-                             int pos0, double theta, fpx_stream_t stream) {
-  FPX_BIND(stream);
+static int rope_launch(void *x, int64_t x_sb, int64_t x_sl, int64_t x_sh, int B, int L, int heads, int d,
+                       int pos0, const int32_t *pos_dev, double theta, cudaStream_t stream) {
   if (!x || B <= 0 || L <= 0 || heads <= 0) return FPX_ERR_INVALID;
   if (d != kHeadDim) return FPX_ERR_UNSUPPORTED;
   RopeParams p{};
   p.x = static_cast<__nv_bfloat16 *>(x);
-  p.sb = x_sb; p.sl = x_sl; p.sh = x_sh; p.L = L; p.heads = heads; p.pos0 = pos0;
+  p.sb = x_sb; p.sl = x_sl; p.sh = x_sh; p.L = L; p.heads = heads; p.pos0 = pos0; p.pos_dev = pos_dev;
   for (int i = 0; i < 64; ++i) {
     // HF: 1 / theta ** (arange(0, d, 2) / d), evaluated in fp32.
     const float expo = (float)(2 * i) / (float)d;
@@ -146,6 +146,19 @@ extern "C" int fpx_rope_neox(void *x, int64_t x_sb, int64_t x_sl, int64_t x_sh, 
   rope_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(p);
   FPX_CHECK_LAUNCH();
   return FPX_OK;
+}
+
+extern "C" int fpx_rope_neox(void *x, int64_t x_sb, int64_t x_sl, int64_t x_sh, int B, int L, int heads, int d,
+                             int pos0, double theta, fpx_stream_t stream) {
+  FPX_BIND(stream);
+  return rope_launch(x, x_sb, x_sl, x_sh, B, L, heads, d, pos0, nullptr, theta, stream);
+}
+
+extern "C" int fpx_rope_neox_at(void *x, int64_t x_sb, int64_t x_sl, int64_t x_sh, int B, int L, int heads,
+                                int d, const int32_t *pos0, double theta, fpx_stream_t stream) {
+  FPX_BIND(stream);
+  if (!pos0) return FPX_ERR_INVALID;
+  return rope_launch(x, x_sb, x_sl, x_sh, B, L, heads, d, 0, pos0, theta, stream);
 }
 
 extern "C" int fpx_silu_mul(const void *gate_up, int64_t rows, int inter, void *out, fpx_stream_t stream) {

@@ -33,7 +33,18 @@ import torch
 
 from . import decode as _decode
 from . import ops
-from ._capi import FpxError, call, ptr, stream, strides3
+from ._capi import FpxError, call, lib, ptr, stream, strides3
+
+
+@dataclass
+class _GraphStep:
+    """Device state of a captured decode step: the new token's position (int32 for the kernels,
+    int64 for the cache write), the key count after it, the input token and the decode workspace."""
+    pos32: torch.Tensor
+    pos64: torch.Tensor
+    keys32: torch.Tensor
+    token: torch.Tensor
+    ws: torch.Tensor
 
 
 @dataclass(frozen=True)
@@ -163,8 +174,12 @@ class Qwen2Model:
         return out
 
     def _rope(self, t, pos0):
-        call("fpx_rope_neox", ptr(t), *strides3(t), t.shape[0], t.shape[1], t.shape[2], t.shape[3], pos0,
-             self.cfg.rope_theta, stream(self.device))
+        if isinstance(pos0, torch.Tensor):  # device position (captured decode step)
+            call("fpx_rope_neox_at", ptr(t), *strides3(t), t.shape[0], t.shape[1], t.shape[2], t.shape[3],
+                 ptr(pos0), self.cfg.rope_theta, stream(self.device))
+        else:
+            call("fpx_rope_neox", ptr(t), *strides3(t), t.shape[0], t.shape[1], t.shape[2], t.shape[3], pos0,
+                 self.cfg.rope_theta, stream(self.device))
 
     def _silu_mul(self, gu):
         rows, two_i = gu.shape
@@ -182,8 +197,9 @@ class Qwen2Model:
         self.k_cache = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
         self.v_cache = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
 
-    def _layer(self, i, h, x, pos0, length, decoding):
-        """One decoder layer: x = normed input rows; returns (h, partial down output)."""
+    def _layer(self, i, h, x, pos0, length, decoding, step=None):
+        """One decoder layer: x = normed input rows; returns (h, partial down output). ``step``
+        (a _GraphStep) replaces the host position by device tensors, for captured decode steps."""
         cfg, lw = self.cfg, self.layers[i]
         d = cfg.head_dim
         hq, hkv = len(self.qh), len(self.kv)
@@ -191,6 +207,21 @@ class Qwen2Model:
         q = qkv[:, : hq * d].view(1, length, hq, d)
         k = qkv[:, hq * d:(hq + hkv) * d].view(1, length, hkv, d)
         v = qkv[:, (hq + hkv) * d:].view(1, length, hkv, d)
+        if step is not None:
+            self._rope(q, step.pos32)
+            self._rope(k, step.pos32)
+            self.k_cache[i, 0].index_copy_(0, step.pos64, k[0])
+            self.v_cache[i, 0].index_copy_(0, step.pos64, v[0])
+            attn = torch.empty_like(q)
+            call("fpx_decode_attention_at", ptr(q), *strides3(q), ptr(self.k_cache[i]), *strides3(self.k_cache[i]),
+                 ptr(self.v_cache[i]), *strides3(self.v_cache[i]), 1, length, self.k_cache.shape[2],
+                 ptr(step.keys32), hq, hkv, d, float(self.scale), ptr(attn), *strides3(attn), None,
+                 ptr(step.ws), step.ws.numel(), stream(self.device))
+            o = self._all_reduce(attn.view(length, hq * d) @ lw.w_o.t())
+            x2 = self._rmsnorm(o, lw.ln2, residual=h)
+            gu = x2 @ lw.w_gu.t()
+            down = self._all_reduce(self._silu_mul(gu) @ lw.w_down.t())
+            return h, down
         self._rope(q, pos0)
         self._rope(k, pos0)
         self.k_cache[i, :, pos0:pos0 + length] = k
@@ -207,7 +238,7 @@ class Qwen2Model:
         down = self._all_reduce(self._silu_mul(gu) @ lw.w_down.t())
         return h, down
 
-    def _forward(self, ids, pos0, decoding):
+    def _forward(self, ids, pos0, decoding, step=None):
         length = ids.shape[0]
         h = torch.nn.functional.embedding(ids, self.embed)
         x = self._rmsnorm(h, self.layers[0].ln1)
@@ -215,7 +246,7 @@ class Qwen2Model:
         for i in range(self.cfg.num_hidden_layers):
             if i > 0:
                 x = self._rmsnorm(down, self.layers[i].ln1, residual=h)  # h += down
-            h, down = self._layer(i, h, x, pos0, length, decoding)
+            h, down = self._layer(i, h, x, pos0, length, decoding, step)
         last = self._rmsnorm(down[-1:].contiguous(), self.norm, residual=h[-1:].contiguous())
         logits = (last @ self.lm_head.t()).float()  # bf16 LM head, as HF's lm_head
         return logits[-1]
@@ -239,6 +270,53 @@ class Qwen2Model:
         logits = self._forward(token.view(1), self.length, decoding=True)
         self.length += 1
         return logits.argmax()
+
+    @torch.inference_mode()
+    def decode_graph(self, first_token: torch.Tensor, steps: int):
+        """``steps`` greedy decode tokens after ``prefill`` (the first is ``first_token``), the
+        same computation as ``decode_step`` but each step one replay of a CUDA graph: the step's
+        position and key count live in device memory and advance inside the graph, and the next
+        token is written back into the graph's input, so no step waits for the host. Returns the
+        [steps] int64 tokens on the device."""
+        cap = self.k_cache.shape[2]
+        if self.length + steps - 1 > cap:
+            raise ValueError("KV cache too small: prefill with max_new_tokens >= steps")
+        dev = self.device
+        out = torch.empty(steps, dtype=torch.int64, device=dev)
+        out[0] = first_token.view(())
+        if steps == 1:
+            return out
+        cfg = self.cfg
+        need = int(lib().fpx_decode_workspace_bytes(1, 1, len(self.qh), len(self.kv), cap, cfg.head_dim))
+        step = _GraphStep(
+            pos32=torch.tensor([self.length], dtype=torch.int32, device=dev),
+            pos64=torch.tensor([self.length], dtype=torch.int64, device=dev),
+            keys32=torch.tensor([self.length + 1], dtype=torch.int32, device=dev),
+            token=first_token.view(1).clone(),
+            ws=torch.empty(max(need, 256), dtype=torch.uint8, device=dev))
+
+        def one_step():
+            logits = self._forward(step.token, None, decoding=True, step=step)
+            step.token.copy_(logits.argmax().view(1))
+            step.pos32.add_(1)
+            step.pos64.add_(1)
+            step.keys32.add_(1)
+
+        side = torch.cuda.Stream(device=dev)  # the eager first step warms the allocator up
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            one_step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        out[1] = step.token[0]
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            one_step()
+        for i in range(2, steps):
+            graph.replay()
+            out[i] = step.token[0]
+        del graph  # a graph holding NCCL calls must go before the process group
+        self.length += steps - 1
+        return out
 
     @torch.inference_mode()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int):

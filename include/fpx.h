@@ -212,6 +212,10 @@ int fpx_rmsnorm(const void *x, const void *residual, const void *weight, double 
  * pos0 .. pos0 + L - 1, inv_freq = theta^(-2i/128) (HF apply_rotary_pos_emb rounding). */
 int fpx_rope_neox(void *x, int64_t x_sb, int64_t x_sl, int64_t x_sh, int B, int L, int heads, int d, int pos0,
                   double theta, fpx_stream_t stream);
+/* fpx_rope_neox with the position of row 0 read from device memory (no reference counterpart;
+ * for captured decode steps). */
+int fpx_rope_neox_at(void *x, int64_t x_sb, int64_t x_sl, int64_t x_sh, int B, int L, int heads, int d,
+                     const int32_t *pos0, double theta, fpx_stream_t stream);
 
 /* SwiGLU: out[r, j] = silu(gate_up[r, j]) * gate_up[r, inter + j] (bf16, HF Qwen2MLP rounding). */
 int fpx_silu_mul(const void *gate_up, int64_t rows, int inter, void *out, fpx_stream_t stream);
@@ -232,6 +236,15 @@ int fpx_decode_attention(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh
                          int B, int Lq, int S, int H, int Hkv, int d, double scale,
                          void *out, int64_t o_sb, int64_t o_sl, int64_t o_sh, float *lse,
                          void *workspace, size_t workspace_bytes, fpx_stream_t stream);
+
+/* fpx_decode_attention with the key count read from device memory (*S_keys <= S_max, no
+ * reference counterpart): the launches do not change between decode steps, so a step can be
+ * captured once in a CUDA graph and replayed. The workspace is sized for S_max. */
+int fpx_decode_attention_at(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh, const void *k, int64_t k_sb,
+                            int64_t k_sl, int64_t k_sh, const void *v, int64_t v_sb, int64_t v_sl, int64_t v_sh,
+                            int B, int Lq, int S_max, const int32_t *S_keys, int H, int Hkv, int d, double scale,
+                            void *out, int64_t o_sb, int64_t o_sl, int64_t o_sh, float *lse, void *workspace,
+                            size_t workspace_bytes, fpx_stream_t stream);
 
 /* Decode that allocates nothing and takes no workspace. No counterpart in the reference: it
  * exists for callers that cannot allocate device memory where they decode (an engine that

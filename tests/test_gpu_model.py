@@ -82,3 +82,20 @@ def test_prefill_matches_hf_with_backend_mean_native():
         mine.prefill(ids)
         out = mine._forward(ids, 0, decoding=False)
     close(out, ref)
+
+
+def test_graph_decode_matches_eager_decode():
+    """decode_graph (each step one CUDA-graph replay, position and key count on the device)
+    yields the same greedy tokens as decode_step."""
+    ids = torch.randint(0, CFG.vocab_size, (600,), generator=torch.Generator().manual_seed(9)).cuda()
+    settings = AttentionSettings("mean_native", 0.08)
+    eager_model = Qwen2Model(CFG, seed=11, attention=settings)
+    graph_model = Qwen2Model(CFG, seed=11, attention=settings)
+    with torch.inference_mode():
+        tokens = [eager_model.prefill(ids, max_new_tokens=8)]
+        for _ in range(7):
+            tokens.append(eager_model.decode_step(tokens[-1]))
+        first = graph_model.prefill(ids, max_new_tokens=8)
+        graph = graph_model.decode_graph(first, 8)
+    assert torch.equal(torch.stack(tokens), graph)
+    assert graph_model.length == eager_model.length == 607
