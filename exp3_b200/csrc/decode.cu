@@ -3,9 +3,10 @@
 // enable_gqa=True) does (attention.py:178-189).
 //
 // Split-K flash decode. Pass 1: one CTA per (key split, KV head, batch x query row) streams
-// its keys 64 at a time through a two-stage cp.async pipeline in shared memory, scores them
-// for all G query heads of the KV group (each K/V row is read once for the whole group), keeps
-// an online softmax per head and writes a partial (o, m, l) per split. Pass 2 merges the
+// its keys 64 at a time through a two-stage cp.async pipeline in shared memory and runs them
+// through mma.sync tiles with the G query heads of the KV group as the rows (each K/V row is
+// read once for the whole group); every warp keeps an online softmax over its quarter of the
+// keys, and the warps' partials are merged into one (o, m, l) per split. Pass 2 merges the
 // splits into bf16 O and a natural-log LSE.
 #include <algorithm>
 #include <mutex>
@@ -30,56 +31,78 @@ struct DecodeParams {
   float *part_ml; // [B*Lq][H][splits][2]
 };
 
-constexpr int kDecodeChunk = 64;   // keys per pipeline stage
-constexpr int kDecodeKPad = 136;   // bf16 per staged K row (272 B: rows start on distinct banks)
+constexpr int kDecodeChunk = 64;   // keys per pipeline stage: 16 per warp
 constexpr int kMaxSplits = 1024;
 
+// XOR-swizzled [rows][128] bf16 tile: 16-byte chunk c of row r lives at chunk c ^ (r & 7).
+FPX_INLINE int dswz(int r, int chunk) { return r * kHeadDim + ((chunk ^ (r & 7)) << 3); }
+
 struct DecodeSmem {
-  __nv_bfloat16 k[2][kDecodeChunk][kDecodeKPad];
-  __nv_bfloat16 v[2][kDecodeChunk][kHeadDim];
-  float qs[kMaxGroup][kHeadDim];
-  float ss[kMaxGroup][kDecodeChunk];
-  float mrow[kMaxGroup], lrow[kMaxGroup], corr[kMaxGroup];
+  __nv_bfloat16 q[16 * kHeadDim];  // the group's query rows (rows >= G zero), swizzled
+  union {
+    struct {
+      __nv_bfloat16 k[2][kDecodeChunk * kHeadDim];  // swizzled K / V stages
+      __nv_bfloat16 v[2][kDecodeChunk * kHeadDim];
+    } stage;
+    struct {
+      float o[4][16][kHeadDim];  // each warp's O for the 16 rows
+      float m[4][16], l[4][16];
+    } merge;
+  } u;
 };
 
+// Decode on the tensor core (mma.sync m16n8k16, bf16 in, fp32 accumulate): the G query heads of
+// the KV group are the M = 16 rows (padded), keys stream 64 per stage through shared memory and
+// warp w takes keys 16w..16w+15 of every stage with its own online softmax (exp2 units); P is
+// rounded to bf16 for P.V. At the end the four warps' (m, l, O) are merged into the split's
+// partial.
 __global__ void __launch_bounds__(128) decode_split_kernel(DecodeParams p) {
   const int split = blockIdx.x, kvh = blockIdx.y, bq = blockIdx.z;
   const int b = bq / p.Lq, row = bq % p.Lq;
   const int G = p.group, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int g8 = lane >> 2, tq = lane & 3;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
   DecodeSmem &sh = *reinterpret_cast<DecodeSmem *>(smem_raw);
-  for (int i = tid; i < G * kHeadDim; i += 128) {
-    const int g = i / kHeadDim, c = i % kHeadDim;
-    const int h = kvh * G + g;
-    sh.qs[g][c] = __bfloat162float(p.q[b * p.q_sb + (int64_t)row * p.q_sl + h * p.q_sh + c]) * p.scale_log2;
+  for (int i = tid; i < 16 * 16; i += 128) {  // 16 rows x 16 chunks of 8 bf16
+    const int r = i >> 4, ch = i & 15;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (r < G)
+      val = *reinterpret_cast<const uint4 *>(p.q + b * p.q_sb + (int64_t)row * p.q_sl + (kvh * G + r) * p.q_sh + 8 * ch);
+    *reinterpret_cast<uint4 *>(&sh.q[dswz(r, ch)]) = val;
   }
-  if (tid < G) { sh.mrow[tid] = -INFINITY; sh.lrow[tid] = 0.f; }
-  float o[kMaxGroup];
-#pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) o[g] = 0.f;
   const int S = p.S_dev ? min(*p.S_dev, p.S) : p.S;
   const int k0 = split * p.keys_per_split;
   const int k1 = min(S, k0 + p.keys_per_split);
   const int chunks = k1 > k0 ? (k1 - k0 + kDecodeChunk - 1) / kDecodeChunk : 0;
   const __nv_bfloat16 *kbase = p.k + b * p.k_sb + kvh * p.k_sh;
   const __nv_bfloat16 *vbase = p.v + b * p.v_sb + kvh * p.v_sh;
-  // Stage chunk c's K and V rows (16-byte cp.async, rows past k1 zero-filled).
   auto stage = [&](int c) {
     const int st = c & 1, base = k0 + c * kDecodeChunk;
     for (int i = tid; i < kDecodeChunk * 16; i += 128) {
       const int r = i >> 4, ch = i & 15;
       const bool ok = base + r < k1;
       const int64_t key = ok ? base + r : k0;
-      cp_async16(&sh.k[st][r][8 * ch], kbase + key * p.k_sl + 8 * ch, ok);
-      cp_async16(&sh.v[st][r][8 * ch], vbase + key * p.v_sl + 8 * ch, ok);
+      cp_async16(&sh.u.stage.k[st][dswz(r, ch)], kbase + key * p.k_sl + 8 * ch, ok);
+      cp_async16(&sh.u.stage.v[st][dswz(r, ch)], vbase + key * p.v_sl + 8 * ch, ok);
     }
     cp_async_commit();
   };
   if (chunks > 0) stage(0);
   __syncthreads();
+  uint32_t qf[8][4];
+  {
+    const int m = lane >> 3;
+    const int r = ((m & 1) << 3) + (lane & 7);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+      ldmatrix_x4(qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], smem_u32(&sh.q[dswz(r, 2 * kk + (m >> 1))]));
+  }
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
   for (int c = 0; c < chunks; ++c) {
     const int st = c & 1;
-    const int n = min(kDecodeChunk, k1 - (k0 + c * kDecodeChunk));
     if (c + 1 < chunks) {
       stage(c + 1);
       cp_async_wait<1>();
@@ -87,74 +110,110 @@ __global__ void __launch_bounds__(128) decode_split_kernel(DecodeParams p) {
       cp_async_wait<0>();
     }
     __syncthreads();
-    // Scores: two threads per key, each over 64 dimensions, halves joined by a shuffle.
-    {
-      const int j = tid >> 1, half = tid & 1;
-      float acc[kMaxGroup];
+    const __nv_bfloat16 *ck = sh.u.stage.k[st], *cv = sh.u.stage.v[st];
+    const int key0 = k0 + c * kDecodeChunk + 16 * warp;  // this warp's 16 keys
+    float sacc[2][4];
 #pragma unroll
-      for (int g = 0; g < kMaxGroup; ++g) acc[g] = 0.f;
-      const uint4 *kr = reinterpret_cast<const uint4 *>(&sh.k[st][j][64 * half]);
+    for (int nt = 0; nt < 2; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint4 u = kr[i];
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    for (int kk2 = 0; kk2 < 4; ++kk2) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 kv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[e]));
-          const int col = 64 * half + 8 * i + 2 * e;
-#pragma unroll
-          for (int g = 0; g < kMaxGroup; ++g)
-            if (g < G) acc[g] = fmaf(sh.qs[g][col], kv.x, fmaf(sh.qs[g][col + 1], kv.y, acc[g]));
-        }
-      }
-#pragma unroll
-      for (int g = 0; g < kMaxGroup; ++g) {
-        if (g < G) {
-          const float tot = acc[g] + __shfl_xor_sync(0xffffffffu, acc[g], 1);
-          if (half == 0) sh.ss[g][j] = j < n ? tot : -INFINITY;
-        }
+      for (int nt = 0; nt < 2; ++nt) {
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(b0, b1, b2, b3, smem_u32(ck + dswz(16 * warp + 8 * nt + (lane & 7), 4 * kk2 + (lane >> 3))));
+        mma_bf16_16816(sacc[nt], qf[2 * kk2], b0, b1);
+        mma_bf16_16816(sacc[nt], qf[2 * kk2 + 1], b2, b3);
       }
     }
-    __syncthreads();
-    // Online softmax per head: warp w owns heads w, w + 4, ...; lane covers keys lane, lane + 32.
-    for (int g = warp; g < G; g += 4) {
-      const float a = sh.ss[g][lane], bb = sh.ss[g][lane + 32];
-      const float m = warp_max(fmaxf(a, bb));
-      const float mn = fmaxf(sh.mrow[g], m);
-      const float ea = a == -INFINITY ? 0.f : exp2f(a - mn), eb = bb == -INFINITY ? 0.f : exp2f(bb - mn);
-      sh.ss[g][lane] = ea;
-      sh.ss[g][lane + 32] = eb;
-      const float l = warp_sum(ea + eb);
-      if (lane == 0) {
-        const float cr = sh.mrow[g] == -INFINITY ? 0.f : exp2f(sh.mrow[g] - mn);
-        sh.corr[g] = cr;
-        sh.lrow[g] = sh.lrow[g] * cr + l;
-        sh.mrow[g] = mn;
+    float mx[2] = {mrow[0], mrow[1]};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = key0 + 8 * nt + 2 * tq + (e & 1);
+        const float x = key < k1 ? sacc[nt][e] * p.scale_log2 : -INFINITY;
+        sacc[nt][e] = x;
+        mx[e >> 1] = fmaxf(mx[e >> 1], x);
       }
+    float corr[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      corr[r] = (mrow[r] == -INFINITY) ? (mx[r] == -INFINITY ? 1.f : 0.f) : exp2f(mrow[r] - mx[r]);
+      mrow[r] = mx[r];
     }
-    __syncthreads();
-    // O += P V: thread = output dimension.
+    float rs[2] = {0.f, 0.f};
+    uint32_t pa[4];
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g)
-      if (g < G) o[g] *= sh.corr[g];
-#pragma unroll 8
-    for (int j = 0; j < kDecodeChunk; ++j) {
-      const float vv = __bfloat162float(sh.v[st][j][tid]);
+    for (int nt = 0; nt < 2; ++nt) {
+      float pv[4];
 #pragma unroll
-      for (int g = 0; g < kMaxGroup; ++g)
-        if (g < G) o[g] = fmaf(sh.ss[g][j], vv, o[g]);
+      for (int e = 0; e < 4; ++e) {
+        const float m = mx[e >> 1];
+        pv[e] = (m == -INFINITY) ? 0.f : exp2f(sacc[nt][e] - m);
+        rs[e >> 1] += pv[e];
+      }
+      pa[nt * 2 + 0] = pack_bf16(pv[0], pv[1]);
+      pa[nt * 2 + 1] = pack_bf16(pv[2], pv[3]);
+    }
+    lrow[0] = lrow[0] * corr[0] + rs[0];
+    lrow[1] = lrow[1] * corr[1] + rs[1];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      o[i][0] *= corr[0]; o[i][1] *= corr[0];
+      o[i][2] *= corr[1]; o[i][3] *= corr[1];
+    }
+    const int vr = 16 * warp + (lane & 7) + (((lane >> 3) & 1) << 3);
+#pragma unroll
+    for (int dn2 = 0; dn2 < 8; ++dn2) {
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4_trans(b0, b1, b2, b3, smem_u32(cv + dswz(vr, 2 * dn2 + (lane >> 4))));
+      mma_bf16_16816(o[2 * dn2], pa, b0, b1);
+      mma_bf16_16816(o[2 * dn2 + 1], pa, b2, b3);
     }
     __syncthreads();  // stage st is refilled by the next iteration's prefetch
   }
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
-    if (g >= G) break;
-    const int h = kvh * G + g;
+  for (int r = 0; r < 2; ++r) {
+    lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+    lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+  }
+  // Merge the four warps (the staging buffers are free now).
+  if (tq == 0) {
+    sh.u.merge.m[warp][g8] = mrow[0];
+    sh.u.merge.m[warp][g8 + 8] = mrow[1];
+    sh.u.merge.l[warp][g8] = lrow[0];
+    sh.u.merge.l[warp][g8 + 8] = lrow[1];
+  }
+#pragma unroll
+  for (int dt = 0; dt < 16; ++dt) {
+    const int col = 8 * dt + 2 * tq;
+    sh.u.merge.o[warp][g8][col] = o[dt][0];
+    sh.u.merge.o[warp][g8][col + 1] = o[dt][1];
+    sh.u.merge.o[warp][g8 + 8][col] = o[dt][2];
+    sh.u.merge.o[warp][g8 + 8][col + 1] = o[dt][3];
+  }
+  __syncthreads();
+  for (int r = 0; r < G; ++r) {
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, sh.u.merge.m[w][r]);
+    float ll = 0.f, oo = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = sh.u.merge.m[w][r];
+      if (mw == -INFINITY) continue;
+      const float sc = exp2f(mw - mm);
+      ll += sh.u.merge.l[w][r] * sc;
+      oo += sh.u.merge.o[w][r][tid] * sc;
+    }
+    const int h = kvh * G + r;
     const int64_t slot = ((int64_t)bq * p.H + h) * p.splits + split;
-    p.part_o[slot * kHeadDim + tid] = o[g];
+    p.part_o[slot * kHeadDim + tid] = oo;
     if (tid == 0) {
-      p.part_ml[2 * slot] = sh.mrow[g];
-      p.part_ml[2 * slot + 1] = sh.lrow[g];
+      p.part_ml[2 * slot] = mm;
+      p.part_ml[2 * slot + 1] = ll;
     }
   }
 }
@@ -176,14 +235,14 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeParams p) {
     l += p.part_ml[2 * (base + s) + 1] * ws;
   }
   l = block_sum<128>(l, red);  // its barriers also publish w[]
-  float o0 = 0.f, o1 = 0.f;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // eight loads in flight
   int s = 0;
-  for (; s + 1 < p.splits; s += 2) {
-    o0 += p.part_o[(base + s) * kHeadDim + threadIdx.x] * w[s];
-    o1 += p.part_o[(base + s + 1) * kHeadDim + threadIdx.x] * w[s + 1];
+  for (; s + 8 <= p.splits; s += 8) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += p.part_o[(base + s + e) * kHeadDim + threadIdx.x] * w[s + e];
   }
-  if (s < p.splits) o0 += p.part_o[(base + s) * kHeadDim + threadIdx.x] * w[s];
-  const float o = o0 + o1;
+  for (; s < p.splits; ++s) acc[0] += p.part_o[(base + s) * kHeadDim + threadIdx.x] * w[s];
+  const float o = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
   const float inv = l > 0.f ? 1.f / l : 0.f;
   p.out[b * p.o_sb + (int64_t)row * p.o_sl + h * p.o_sh + threadIdx.x] = __float2bfloat16_rn(o * inv);
   if (p.lse && threadIdx.x == 0)
@@ -227,8 +286,10 @@ static int decode_run(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh, c
   if (d != kHeadDim) return FPX_ERR_UNSUPPORTED;
   if (!q || !k || !v || !out || B <= 0 || Lq <= 0 || S <= 0 || H <= 0 || Hkv <= 0)
     return FPX_ERR_INVALID;
-  if (H % Hkv || H / Hkv > kMaxGroup || k_sl % 8 || k_sb % 8 || k_sh % 8 ||
-      (reinterpret_cast<uintptr_t>(k) & 15))
+  // Q, K and V rows move in 16-byte pieces: last dim contiguous, other strides multiples of 8.
+  if (H % Hkv || H / Hkv > kMaxGroup || k_sl % 8 || k_sb % 8 || k_sh % 8 || v_sl % 8 || v_sb % 8 ||
+      v_sh % 8 || q_sl % 8 || q_sb % 8 || q_sh % 8 || (reinterpret_cast<uintptr_t>(k) & 15) ||
+      (reinterpret_cast<uintptr_t>(v) & 15) || (reinterpret_cast<uintptr_t>(q) & 15))
     return FPX_ERR_SHAPE;
   const size_t need = fpx_decode_workspace_bytes(B, Lq, H, Hkv, S, d);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
@@ -327,8 +388,10 @@ extern "C" int fpx_decode_attention_noalloc(const void *q, int64_t q_sb, int64_t
   if (d != kHeadDim) return FPX_ERR_UNSUPPORTED;
   if (!q || !k || !v || !out || B <= 0 || Lq <= 0 || S <= 0 || H <= 0 || Hkv <= 0)
     return FPX_ERR_INVALID;
-  if (H % Hkv || H / Hkv > kMaxGroup || k_sl % 8 || k_sb % 8 || k_sh % 8 ||
-      (reinterpret_cast<uintptr_t>(k) & 15))
+  // Q, K and V rows move in 16-byte pieces: last dim contiguous, other strides multiples of 8.
+  if (H % Hkv || H / Hkv > kMaxGroup || k_sl % 8 || k_sb % 8 || k_sh % 8 || v_sl % 8 || v_sb % 8 ||
+      v_sh % 8 || q_sl % 8 || q_sb % 8 || q_sh % 8 || (reinterpret_cast<uintptr_t>(k) & 15) ||
+      (reinterpret_cast<uintptr_t>(v) & 15) || (reinterpret_cast<uintptr_t>(q) & 15))
     return FPX_ERR_SHAPE;
   // Sizes whose partials do not fit the fixed array are refused before anything runs.
   if (fpx_decode_workspace_bytes(B, Lq, H, Hkv, S, d) > kDecodeScratchBytes) return FPX_ERR_WORKSPACE;
