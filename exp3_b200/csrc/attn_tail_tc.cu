@@ -321,14 +321,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale_log2;
       const float mn = fmaxf(m, bmax);
       float corr = 1.f;
-      const bool move = __any_sync(0xffffffffu, mn > m + kRescaleThreshold || m == -INFINITY);
+      // Each row decides for itself (rows never influence one another's rounding); rows that
+      // keep their max rescale O by exactly 1 when another row of the warp moves.
+      const bool move = mn > m + kRescaleThreshold || m == -INFINITY;
       if (move) {
         corr = (m == -INFINITY) ? 0.f : ex2(m - mn);
         l *= corr;
         m = mn;
       }
       l += tail_row(sv, scale_log2, -m, s_addr);
-      if (move && i > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+      if (i > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float o[32];

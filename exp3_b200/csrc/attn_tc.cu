@@ -68,7 +68,7 @@ struct alignas(1024) Smem {
   uint64_t q_full, k_full[kKStages], k_empty[kKStages], v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], p_full[2], o_done[2], drain;
   uint32_t tmem_base;
-  int abort, n_union;
+  int abort, n_union, n_tile[2], diag_tile[2];
   uint32_t bits[2][kMaxBlocks / 32];
   uint16_t u_blk[kMaxBlocks];
   uint8_t u_flags[kMaxBlocks];
@@ -145,15 +145,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int heads[2] = {hA, hA + 1};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool failed = *reinterpret_cast<volatile int *>(&g_device_error) != 0;
+  // Block lists: the fused path's compact lists, or the reference's [B, nb, nb, H] int64
+  // indices with [B, nb, H] counts (fpx_exact_attention); entries past the tile are dropped,
+  // as the reference's causal mask leaves them no key.
+  const bool ref = p.ref_indices != nullptr;
+  const int nb = ref ? p.nb : p.route.nb;
   int cnt[2];
   const int32_t *lists[2];
   for (int x = 0; x < 2; ++x) {
     const bool live = x == 0 || has_b;
-    const int64_t rr = p.route.row(b, live ? heads[x] : hA, t, p.H);
-    cnt[x] = (live && !failed) ? p.route.counts[rr] : 0;
-    lists[x] = p.route.lists + rr * p.route.nb;
+    const int h = live ? heads[x] : hA;
+    const int64_t rr = ref ? 0 : p.route.row(b, h, t, p.H);
+    cnt[x] = (live && !failed) ? (ref ? p.ref_counts[((int64_t)b * nb + t) * p.H + h] : p.route.counts[rr]) : 0;
+    cnt[x] = min(max(cnt[x], 0), nb);
+    lists[x] = ref ? nullptr : p.route.lists + rr * p.route.nb;
   }
-  const int words = (p.route.nb + 31) / 32;
+  const int words = (nb + 31) / 32;
 
   if (threadIdx.x == 0) {
     mbar_init(&sh.q_full, 1);
@@ -182,8 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   for (int x = 0; x < 2; ++x)
     for (int i = threadIdx.x; i < cnt[x]; i += kThreads) {
-      const int blk = lists[x][i];
-      atomicOr(&sh.bits[x][blk >> 5], 1u << (blk & 31));
+      const int blk = ref ? (int)p.ref_indices[(((int64_t)b * nb + t) * nb + i) * p.H + heads[x]] : lists[x][i];
+      if (blk >= 0 && blk <= t) atomicOr(&sh.bits[x][blk >> 5], 1u << (blk & 31));
     }
   __syncthreads();
   if (warp == 8) {  // union of the two lists, ascending, with per-tile flags
@@ -209,6 +216,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       base += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) sh.n_union = base;
+    // Per tile: the number of blocks it runs and whether the diagonal block is among them
+    // (ascending order puts it last).
+    for (int x = 0; x < 2; ++x) {
+      int nx = 0;
+      for (int w = lane; w < words; w += 32) nx += __popc(sh.bits[x][w]);
+      nx = __reduce_add_sync(0xffffffffu, nx);
+      if (lane == 0) {
+        sh.n_tile[x] = nx;
+        sh.diag_tile[x] = (sh.bits[x][t >> 5] >> (t & 31)) & 1u;
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -328,11 +346,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t o_addr = tmem + lane_off + 256 + 128 * x;
     const bool live = x == 0 || has_b;
     const int h = heads[x];
-    const int n = cnt[x];
+    const int n = sh.n_tile[x];
     const int qrow = t * 128 + r;
     const float sl2 = p.scale_log2;
-    // Lists are ascending and end at most at t, so only the last block can be the diagonal.
-    const bool last_is_diag = n > 0 && lists[x][n - 1] == t;
+    // Blocks run in ascending order and end at most at t, so only the last can be the diagonal.
+    const bool last_is_diag = n > 0 && sh.diag_tile[x];
     float m = -INFINITY, l = 0.f;
     bool ok = live;
     for (int i = 0; i < n && ok; ++i) {
@@ -359,7 +377,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
       const float mn = fmaxf(m, bmax);
       float corr = 1.f;
-      const bool move = __any_sync(0xffffffffu, mn > m + kRescaleThreshold || m == -INFINITY);
+      // Each row decides for itself (rows never influence one another's rounding); rows that
+      // keep their max rescale O by exactly 1 when another row of the warp moves.
+      const bool move = mn > m + kRescaleThreshold || m == -INFINITY;
       if (move) {
         corr = (m == -INFINITY) ? 0.f : ex2(m - mn);
         l *= corr;
@@ -369,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The diagonal block's masked entries are -inf: the MUFU returns exactly 0 for them.
       l += diag ? softmax_row<0>(sv, sl2, neg, s_addr) : softmax_row<kEmu>(sv, sl2, neg, s_addr);
       // O_X holds blocks < i and no P.V runs until p_full: rescale it for the moved max.
-      if (move && i > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+      if (i > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float o[32];
@@ -482,7 +502,7 @@ size_t exact_tc_smem() { return sizeof(Smem) + 1024; }
 
 int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s) {
   if (tiles <= 0 || heads <= 0) return FPX_OK;
-  if (p.route.nb > kMaxBlocks) return FPX_ERR_UNSUPPORTED;
+  if ((p.ref_indices ? p.nb : p.route.nb) > kMaxBlocks) return FPX_ERR_UNSUPPORTED;
   CUtensorMap tq, tk, tv, to;
   if (!encode_4d(&tq, p.q, kHeadDim, p.H, L, B, p.q_sh, p.q_sl, p.q_sb) ||
       !encode_4d(&tk, p.k, kHeadDim, Hkv, L, B, p.k_sh, p.k_sl, p.k_sb) ||

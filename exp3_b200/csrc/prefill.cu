@@ -282,7 +282,8 @@ extern "C" int fpx_exact_attention(const void *q, int64_t q_sb, int64_t q_sl, in
   ep.head_begin = 0; ep.tile_begin = 0;
   ep.scale_log2 = (float)scale * kLog2e;
   ep.ref_indices = indices; ep.ref_counts = counts;
-  return launch_exact_mma(ep, kExactRefLayout, nb, H, B, stream);
+  return get_option(kOptExactKernel) == kExactKernelMmaSync ? launch_exact_mma(ep, kExactRefLayout, nb, H, B, stream)
+                                                            : launch_exact_tc(ep, B, L, Hkv, nb, H, stream);
 }
 
 extern "C" int fpx_mean_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,

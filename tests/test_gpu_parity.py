@@ -230,6 +230,22 @@ def test_future_keys_do_not_change_past_outputs():
     assert torch.equal(path(k2, v2)[:, :300], first[:, :300])
 
 
+@pytest.mark.parametrize("method", ["mean_native", "cgf_mean", "fp_v1_rescue_v2"])
+def test_fused_path_is_causal_bit_for_bit(method):
+    """The fused path (routing, tcgen05 exact attention, tails): K/V rows from block 5 on never
+    change rows of tiles 0..4, to the bit (each row's softmax is independent of its warp's
+    other rows)."""
+    shape = synthetic.LayerShape(1, 1000, 8, 2)
+    q, k, v = cuda(*synthetic.attention_inputs(shape, seed=4, needles=2, structured_sigma=0.5))
+    first = ops.prefill_attention(q, k, v, method, 0.08, SCALE)
+    k2, v2 = k.clone(), v.clone()
+    k2[:, 640:] *= 19
+    v2[:, 640:] += 23
+    second = ops.prefill_attention(q, k2, v2, method, 0.08, SCALE)
+    assert torch.equal(second[:, :640], first[:, :640])
+    assert not torch.equal(second[:, 640:], first[:, 640:])
+
+
 def test_decode_matches_dense_softmax():
     g = torch.Generator().manual_seed(9)
     for lq, s_len in ((1, 4097), (3, 300)):
