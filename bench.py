@@ -133,6 +133,26 @@ class ClockSampler:
     def __init__(self, index):
         self.index, self.rows, self.proc, self.nvml, self.max_mhz = index, [], None, None, None
         self.stop = threading.Event()
+        self.opened = False
+
+    def open(self):
+        """NVML start-up and a few discarded reads, before the warm-up steps: the first reads of
+        a fresh process are slow and must not fall inside the timed region."""
+        if self.opened:
+            return self
+        self.opened = True
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            for _ in range(3):
+                self._nvml_sample()
+            self.rows.clear()
+        except Exception:
+            self.nvml = None
+        return self
 
     def _nvml_sample(self):
         n = self.nvml
@@ -143,24 +163,18 @@ class ClockSampler:
         self.rows.append((float(mhz), {name for name, m in zip(self.REASONS, masks) if bits & m}))
 
     def _nvml_loop(self):
-        while not self.stop.wait(0.002):
+        while not self.stop.wait(0.005):
             try:
                 self._nvml_sample()
             except Exception:  # a failed read only loses a sample
                 pass
 
     def __enter__(self):
-        try:
-            import pynvml
-            pynvml.nvmlInit()
-            self.nvml = pynvml
-            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
-            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        self.open()
+        if self.nvml:
             self.thread = threading.Thread(target=self._nvml_loop, daemon=True)
             self.thread.start()
             return self
-        except Exception:
-            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
@@ -272,6 +286,7 @@ def run_model(args, rank, world, local):
                        attention=AttentionSettings(args.method, args.alpha))
     ids_host = synthetic_prompt(args.prompt_length, QWEN25_7B.vocab_size).pin_memory()
     ids = ids_host.to(dev)
+    clocks = ClockSampler(local).open()
     for _ in range(args.warmup):
         model.prefill(ids, args.decode_tokens)
     torch.cuda.synchronize()
@@ -293,7 +308,7 @@ def run_model(args, rank, world, local):
             ms = float(t)
         return ms
 
-    with ClockSampler(local) as clocks:
+    with clocks:
         prefill_ms = timed(lambda: model.prefill(ids, args.decode_tokens), args.steps)
     first = model.prefill(ids, args.decode_tokens)
 
@@ -397,6 +412,7 @@ def main():
         ops.prefill_attention(q, k, v, method, alpha, SCALE, stages=STAGE_MEAN, **common)
         events[3].record()
 
+    clocks = ClockSampler(local).open()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -405,7 +421,7 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with clocks:
         start.record()
         for i in range(args.steps):
             step(ev[i])
