@@ -192,26 +192,6 @@ class Qwen2Model:
             torch.distributed.all_reduce(t, group=self.group)
         return t
 
-    # Prefill row-parallel projections are cut into this many row chunks: each chunk's NCCL
-    # all-reduce (on NCCL's stream) runs while the next chunk's GEMM runs on the compute stream.
-    overlap_chunks = 4
-
-    def _row_parallel(self, a, w):
-        """a @ w.T summed over the tensor-parallel ranks (o_proj, down_proj)."""
-        rows = a.shape[0]
-        if self.tp_size == 1 or rows < 2048 or self.overlap_chunks <= 1:
-            return self._all_reduce(a @ w.t())
-        out = torch.empty(rows, w.shape[0], dtype=a.dtype, device=a.device)
-        step = -(-rows // self.overlap_chunks)
-        works = []
-        for r0 in range(0, rows, step):
-            r1 = min(rows, r0 + step)
-            torch.matmul(a[r0:r1], w.t(), out=out[r0:r1])
-            works.append(torch.distributed.all_reduce(out[r0:r1], group=self.group, async_op=True))
-        for work in works:
-            work.wait()  # the compute stream waits for NCCL's; the host does not block
-        return out
-
     def _alloc_cache(self, capacity):
         shape = (self.cfg.num_hidden_layers, 1, capacity, len(self.kv), self.cfg.head_dim)
         self.k_cache = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
@@ -252,10 +232,10 @@ class Qwen2Model:
         else:
             a = self.attn
             attn = ops.prefill_attention(q, k, v, a.method, a.alpha, self.scale, a.sink, a.window, a.last_full)
-        o = self._row_parallel(attn.view(length, hq * d), lw.w_o)
+        o = self._all_reduce(attn.view(length, hq * d) @ lw.w_o.t())
         x2 = self._rmsnorm(o, lw.ln2, residual=h)  # h += o
         gu = x2 @ lw.w_gu.t()
-        down = self._row_parallel(self._silu_mul(gu), lw.w_down)
+        down = self._all_reduce(self._silu_mul(gu) @ lw.w_down.t())
         return h, down
 
     def _forward(self, ids, pos0, decoding, step=None):

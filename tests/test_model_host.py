@@ -90,35 +90,3 @@ def test_synthetic_prompt_plants_repeated_spans():
     assert ids.shape == (4096,) and int(ids.max()) < 1000
     assert torch.equal(ids, synthetic_prompt(4096, vocab=1000, spans=8, span_len=16, seed=1))
 
-
-def _chunked_rank(rank, world, port, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
-    try:
-        from exp3_b200.model import Qwen2Model
-
-        class Stub:  # the attributes Qwen2Model._row_parallel reads
-            tp_size, group, overlap_chunks = world, None, 4
-            _all_reduce = Qwen2Model._all_reduce
-
-        g = torch.Generator().manual_seed(1)
-        a_full = torch.randn(4100, 64, generator=g)
-        w_full = torch.randn(32, 64, generator=g)
-        cols = slice(32 * rank, 32 * (rank + 1))  # this rank's input features
-        out = Qwen2Model._row_parallel(Stub(), a_full[:, cols].contiguous(), w_full[:, cols].contiguous())
-        q.put((rank, torch.allclose(out, a_full @ w_full.t(), atol=1e-3)))
-    finally:
-        dist.destroy_process_group()
-
-
-def test_chunked_row_parallel_overlap_gloo_world2():
-    """The prefill row-parallel product: row chunks all-reduced asynchronously sum to the full one."""
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    procs = [ctx.Process(target=_chunked_rank, args=(r, 2, 29533, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    results = dict(q.get(timeout=120) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
-    assert results == {0: True, 1: True}
