@@ -47,9 +47,13 @@ constexpr uint32_t kTile = 2 * kHalf;
 constexpr uint32_t kIdesc = idesc_bf16(128, 128, false);
 constexpr float kLn128 = 4.852030263919617f;
 
+// kQ2: the squared-query tiles exist (cgf_mean, dispersion_mean). mean_balanced keeps 96 KB of
+// shared memory and 256 TMEM columns, so two of its CTAs share an SM.
+template <bool kQ2>
 struct alignas(1024) SelSmem {
-  uint8_t q[kTile], q2h[kTile], q2l[kTile];
-  uint8_t ring[2][kTile];
+  uint8_t q[kTile];
+  uint8_t q2h[kQ2 ? kTile : 16], q2l[kQ2 ? kTile : 16];
+  alignas(1024) uint8_t ring[2][kTile];
   uint64_t q_full, q2_full, r_full[2], r_empty[2], acc_full[2], acc_empty[2], drain;
   uint32_t tmem_base;
   int abort;
@@ -88,7 +92,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kTilesPerChunk = kSel == 0 ? 2 : 4;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  SelSmem &sh = *reinterpret_cast<SelSmem *>(smem_raw + pad);
+  constexpr uint32_t kCols = kSel == 0 ? 256 : 512;       // TMEM columns
+  constexpr uint32_t kAccStride = kSel == 0 ? 128 : 256;  // per accumulator buffer
+  SelSmem<(kSel > 0)> &sh = *reinterpret_cast<SelSmem<(kSel > 0)> *>(smem_raw + pad);
   volatile int *abort = &sh.abort;
   const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);
   const int h = p.head_begin + blockIdx.y;
@@ -112,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(&sh.tmem_base, 512);
+    tmem_alloc(&sh.tmem_base, kCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -155,16 +161,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ MMA issuer
     bool ok = !*abort && chunks > 0;
     if (ok) ok = mbar_wait_warp(&sh.q_full, 0, abort);
-    if (ok && kSel > 0) ok = mbar_wait_warp(&sh.q2_full, 0, abort);
+    bool have_q2 = kSel == 0;  // Q^2 is awaited only before its first product
     int n = 0;
     for (int u = 0; u < units && ok; ++u) {
       const bool transposed = u >= chunks;
       const int a = u & 1;
       if (u >= 2 && !(ok = mbar_wait_warp(&sh.acc_empty[a], ((u >> 1) - 1) & 1, abort))) break;
-      const uint32_t acc_l = tmem + 256 * a, acc_u = acc_l + 128;
+      const uint32_t acc_l = tmem + kAccStride * a, acc_u = acc_l + 128;
       for (int j = 0; j < kTilesPerChunk && ok; ++j, ++n) {
         const int s = n & 1;
         if (!(ok = mbar_wait_warp(&sh.r_full[s], (n >> 1) & 1, abort))) break;
+        if (j >= 2 && !have_q2) {
+          if (!(ok = mbar_wait_warp(&sh.q2_full, 0, abort))) break;
+          have_q2 = true;
+        }
         tc_fence_after();
         if (lane == 0) {
           const uint8_t *x = sh.ring[s];
@@ -253,8 +263,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int q2 = 0; q2 < 2; ++q2) {
           const int c0 = 64 * g + 32 * q2;
           float vl[32], vu[32];
-          tmem_ld32(tmem + lane_off + 256 * a + c0, vl);
-          if (kSel > 0) tmem_ld32(tmem + lane_off + 256 * a + 128 + c0, vu);
+          tmem_ld32(tmem + lane_off + kAccStride * a + c0, vl);
+          if (kSel > 0) tmem_ld32(tmem + lane_off + kAccStride * a + 128 + c0, vu);
           tmem_wait_ld();
           float cmax = -INFINITY;
 #pragma unroll
@@ -301,8 +311,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int q2 = 0; q2 < 2; ++q2) {
           const int r0 = 64 * g + 32 * q2;
           float vl[32], vu[32];
-          tmem_ld32(tmem + lane_off + 256 * a + r0, vl);
-          if (kSel > 0) tmem_ld32(tmem + lane_off + 256 * a + 128 + r0, vu);
+          tmem_ld32(tmem + lane_off + kAccStride * a + r0, vl);
+          if (kSel > 0) tmem_ld32(tmem + lane_off + kAccStride * a + 128 + r0, vu);
           tmem_wait_ld();
           float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
@@ -395,11 +405,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && sh.abort) atomicExch(device_error, 1);
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, kCols);
   }
 }
 
-size_t selector_route_tc_smem() { return sizeof(SelSmem) + 1024; }
+template <int kSel>
+size_t selector_route_tc_smem() { return sizeof(SelSmem<(kSel > 0)>) + 1024; }
 
 int launch_selector_route_tc(const SelParams &p, int selector, int tiles, int heads, int B, cudaStream_t s) {
   if (tiles <= 0 || heads <= 0) return FPX_OK;
@@ -416,9 +427,9 @@ int launch_selector_route_tc(const SelParams &p, int selector, int tiles, int he
       !encode_4d(&tvkl, p.vk_lo, d, p.Hkv, p.nb, B, kHeadDim, dstride, bstride))
     return FPX_ERR_INVALID;
   const dim3 grid(tiles, heads, B);
-  const size_t smem = selector_route_tc_smem();
 #define FPX_SEL_TC(K)                                                                                   \
   do {                                                                                                  \
+    const size_t smem = selector_route_tc_smem<K>();                                                    \
     cudaFuncSetAttribute(selector_route_tc_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
     selector_route_tc_kernel<K><<<grid, kThreads, smem, s>>>(tq, tmkh, tmkl, tvkh, tvkl, p, device_error); \
   } while (0)
