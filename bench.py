@@ -52,6 +52,12 @@ LAYER_CONFIGS = {
                metric="effective TFLOP/s of the 64K Qwen2.5-32B-shape prefill attention layer",
                workload="config 5: one attention layer, B=2 L=65536 H=40 Hkv=8 d=128 bf16, synthetic N(0,1) "
                         "Q/K/V + RoPE(theta 1e6), K row norms log-normal(0, 0.5)"),
+    # The reference's head-dim-256 path (check_qwen35_math.py: Qwen3.5-4B full-attention layers,
+    # 16 query heads over 4 KV heads), run with fp_v1 as its Qwen3.5 drivers do.
+    "q35": dict(batch=1, length=32768, heads=16, kv_heads=4, head_dim=256, method="fp_v1",
+                metric="effective TFLOP/s of the 32K Qwen3.5-4B-shape (head dim 256) prefill attention layer",
+                workload="head dim 256: one attention layer, B=1 L=32768 H=16 Hkv=4 d=256 bf16, synthetic N(0,1) "
+                         "Q/K/V + RoPE(theta 1e6) + 32 needles"),
 }
 METRIC = LAYER_CONFIGS["c2"]["metric"]
 WORKLOAD = LAYER_CONFIGS["c2"]["workload"]
@@ -63,17 +69,21 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--method", default="mean_native")
+    ap.add_argument("--method", default=None, help="default: mean_native (fp_v1 for q35)")
     ap.add_argument("--alpha", type=float, default=0.08)
     ap.add_argument("--variant", default="iid", choices=["iid", "structured"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default="c2", choices=sorted(LAYER_CONFIGS),
-                    help="layer workload: c2 (32K, the headline), c4 (128K), c5 (32B shape, B=2, 64K)")
+                    help="layer workload: c2 (32K, the headline), c4 (128K), c5 (32B shape, B=2, 64K), "
+                         "q35 (head dim 256, 32K)")
     ap.add_argument("--workload", default="layer", choices=["layer", "model"],
                     help="layer: the 32K attention layer (default); model: full-model prefill + decode")
     ap.add_argument("--prompt-length", type=int, default=32640)
     ap.add_argument("--decode-tokens", type=int, default=128)
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.method is None:
+        args.method = LAYER_CONFIGS[args.config].get("method", "mean_native")
+    return args
 
 
 def peaks():
@@ -231,7 +241,7 @@ def cpu_sample_tiles(blocks):
     return [blocks - 1, blocks // 2, blocks // 8]
 
 
-def cpu_baseline(method, alpha, q, k, v, budget_s=15.0):
+def cpu_baseline(method, alpha, q, k, v, budget_s=15.0, config="c2"):
     """Times the oracle (the reference algorithm restated on the CPU, fp32 like the reference's
     torch code) with all host threads on a bounded sample of query tiles."""
     import oracle
@@ -244,27 +254,31 @@ def cpu_baseline(method, alpha, q, k, v, budget_s=15.0):
     runs = 0
     while runs == 0 or (elapsed < budget_s and runs < 20):
         t0 = time.perf_counter()
-        outs, sel, _ = oracle.prefill_attention_tiles(method, q, k, v, SCALE, alpha, tiles=tiles)
+        d = q.shape[-1]
+        outs, sel, _ = oracle.prefill_attention_tiles(method, q, k, v, d ** -0.5, alpha, tiles=tiles)
         elapsed += time.perf_counter() - t0
-        flops += 4 * 128 * oracle.exact_token_pairs(sel, q.shape[1])
+        flops += 4 * d * oracle.exact_token_pairs(sel, q.shape[1])
         runs += 1
     return {"value": flops / elapsed / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"query tiles {tiles} of the 32K layer, all 28 heads, {runs} pass(es), "
-                      f"{elapsed:.1f} s, oracle/ fp32 torch on {threads} threads"}
+            "sample": f"query tiles {tiles} of the {config} layer (L={q.shape[1]}), all {q.shape[2]} heads, "
+                      f"{runs} pass(es), {elapsed:.1f} s, oracle/ fp32 torch on {threads} threads"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    q, k, v = inputs(args.variant, "cpu")
+    q, k, v = inputs(args.variant, "cpu", args.config)
     for _ in range(args.warmup):
-        cpu_baseline(args.method, args.alpha, q, k, v, budget_s=0.0)
-    values = [cpu_baseline(args.method, args.alpha, q, k, v, budget_s=0.0) for _ in range(args.steps)]
+        cpu_baseline(args.method, args.alpha, q, k, v, budget_s=0.0, config=args.config)
+    values = [cpu_baseline(args.method, args.alpha, q, k, v, budget_s=0.0, config=args.config)
+              for _ in range(args.steps)]
+    cfg = LAYER_CONFIGS[args.config]
     value = statistics.median(v["value"] for v in values)
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+    line = {"impl": "reference", "metric": cfg["metric"], "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "method": args.method, "alpha": args.alpha, "variant": args.variant},
+            "config": {"workload": cfg["workload"], "method": args.method, "alpha": args.alpha,
+                       "variant": args.variant},
             "cpu_baseline": {**values[0], "value": value},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -379,19 +393,20 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     cfg = LAYER_CONFIGS[args.config]
-    b, length, heads, kv_heads, d = cfg["batch"], cfg["length"], cfg["heads"], cfg["kv_heads"], 128
+    b, length, heads, kv_heads, d = cfg["batch"], cfg["length"], cfg["heads"], cfg["kv_heads"], cfg.get("head_dim", 128)
+    scale = d ** -0.5
     group = heads // kv_heads
     blocks = length // 128
     q, k, v = inputs(args.variant, dev, args.config)
     kv_range, tile_range = partition(rank, world, kv_heads, blocks)
     method, alpha = args.method, args.alpha
-    nbytes = ops.workspace_bytes(method, b, length, heads, kv_heads)
+    nbytes = ops.workspace_bytes(method, b, length, heads, kv_heads, d)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     out = torch.empty(b, length, heads, d, dtype=torch.bfloat16, device=dev)
 
     # Selected work of this rank (routing of the full layer, untimed).
-    ops.prefill_attention(q, k, v, method, alpha, SCALE, out=out, ws=ws, stages=STAGE_ROUTE)
-    selected, _, _ = ops.export_routing(method, b, length, heads, kv_heads, ws=ws, device=dev)
+    ops.prefill_attention(q, k, v, method, alpha, scale, out=out, ws=ws, stages=STAGE_ROUTE)
+    selected, _, _ = ops.export_routing(method, b, length, heads, kv_heads, head_dim=d, ws=ws, device=dev)
     pairs = exact_pairs(selected, length, kv_range, tile_range, group)
     all_pairs = exact_pairs(selected, length, (0, kv_heads), (0, blocks), group)
     density = float(selected.sum()) / (b * heads * blocks * (blocks + 1) / 2)
@@ -402,14 +417,14 @@ def main():
     def step(events=None):
         common = dict(out=out, ws=ws, kv_range=kv_range, tile_range=tile_range)
         if events is None:
-            ops.prefill_attention(q, k, v, method, alpha, SCALE, **common)
+            ops.prefill_attention(q, k, v, method, alpha, scale, **common)
             return
         events[0].record()
-        ops.prefill_attention(q, k, v, method, alpha, SCALE, stages=STAGE_ROUTE, **common)
+        ops.prefill_attention(q, k, v, method, alpha, scale, stages=STAGE_ROUTE, **common)
         events[1].record()
-        ops.prefill_attention(q, k, v, method, alpha, SCALE, stages=STAGE_EXACT, **common)
+        ops.prefill_attention(q, k, v, method, alpha, scale, stages=STAGE_EXACT, **common)
         events[2].record()
-        ops.prefill_attention(q, k, v, method, alpha, SCALE, stages=STAGE_MEAN, **common)
+        ops.prefill_attention(q, k, v, method, alpha, scale, stages=STAGE_MEAN, **common)
         events[3].record()
 
     clocks = ClockSampler(local).open()
@@ -479,9 +494,9 @@ def main():
             compute.wait_event(ready)
             if tile_range == (0, blocks):
                 o, _ = backend.forward(Layer(), qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2), None,
-                                       SCALE)
+                                       scale)
             else:  # a tile shard: the same fused op with this rank's tile range
-                o = ops.prefill_attention(qd, kd, vd, method, alpha, SCALE, tile_range=tile_range)
+                o = ops.prefill_attention(qd, kd, vd, method, alpha, scale, tile_range=tile_range)
             done = torch.cuda.Event()
             done.record(compute)
             in_free[sl] = done
@@ -518,7 +533,7 @@ def main():
     traffic_file = ROOT / "profiles" / "exact_attention_traffic.json"
     if traffic_file.exists():
         try:
-            traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch_c2")
+            traffic = json.loads(traffic_file.read_text()).get(f"bytes_per_launch_{args.config}")
         except ValueError:
             traffic = None
     launches_per_step = {"dense": 2, "fp_v1": 3}.get(method, 4)
@@ -528,9 +543,9 @@ def main():
     line = None
     if rank == 0:
         cpu = None
-        if world == 1 and not args.no_cpu_baseline and args.config == "c2":
+        if world == 1 and not args.no_cpu_baseline and args.config in ("c2", "q35"):
             qc, kc, vc = q.cpu(), k.cpu(), v.cpu()
-            cpu = cpu_baseline(method, alpha, qc, kc, vc)
+            cpu = cpu_baseline(method, alpha, qc, kc, vc, config=args.config)
         line = {
             "metric": cfg["metric"], "value": total_flops / (ms_step * 1e-3) / 1e12, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
@@ -541,7 +556,7 @@ def main():
                        "l2": f"no flush: Q ({q.numel() * 2 / 1e6:.0f} MB) and O are larger than the 126 MB L2",
                        "parallelism": f"{world} rank(s): (KV group x query-tile range) shards, no collective",
                        "stage_ms_rank0": {"route": route_ms, "exact": exact_ms, "mean_merge": mean_ms}},
-            "roofline": {"bound": "tensor", "kernel": "exact attention (sparse FA)", "achieved": achieved,
+            "roofline": {"bound": "tensor", "kernel": "exact attention (sparse FA)" + (", d=256" if d == 256 else ""), "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_kind": f"{peak_kind} burst bf16", "frac_of_sustained":
                              achieved / peak_sus if peak_sus else None, "traffic": traffic},

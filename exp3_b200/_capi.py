@@ -58,6 +58,13 @@ SIGNATURES = {
                                  P, *S3, P, P, c_size, P], c_int),
     "fpx_decode_attention_noalloc": ([P, *S3, P, *S3, P, *S3, c_int, c_int, c_int, c_int, c_int, c_int,
                                       c_double, P, *S3, P, P], c_int),
+    "fpx_ar_buffer_bytes": ([c_int], c_size),
+    "fpx_ar_create": ([c_size, ctypes.POINTER(c_void_p), ctypes.POINTER(ctypes.c_char)], c_int),
+    "fpx_ar_open": ([ctypes.POINTER(ctypes.c_char), ctypes.POINTER(c_void_p)], c_int),
+    "fpx_ar_close": ([P], c_int),
+    "fpx_ar_destroy": ([P], c_int),
+    "fpx_ar_error": ([P, ctypes.POINTER(c_int)], c_int),
+    "fpx_allreduce_bf16": ([P, c_i64, ctypes.POINTER(c_void_p), c_int, c_int, c_int, P], c_int),
     "fpx_rmsnorm": ([P, P, P, c_double, c_i64, c_int, P, P, P], c_int),
     "fpx_rope_neox": ([P, *S3, c_int, c_int, c_int, c_int, c_int, c_double, P], c_int),
     "fpx_rope_neox_at": ([P, *S3, c_int, c_int, c_int, c_int, P, c_double, P], c_int),

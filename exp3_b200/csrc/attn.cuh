@@ -18,11 +18,14 @@ struct ExactParams {
   RouteView route;                  // kExactLists
   const int64_t *ref_indices;       // kExactRefLayout: [B][nb][nb][H]
   const int32_t *ref_counts;        //                  [B][nb][H]
+  int kv_count;                     // KV groups in the launch (set by the d = 256 launcher)
 };
 
 int launch_exact_mma(const ExactParams &p, int mode, int tiles, int heads, int B, cudaStream_t s);
 // tcgen05 / TMEM / TMA exact kernel over internal lists (kExactLists).
 int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s);
+// Head dim 256 (attn_tc256.cu): one query tile per CTA, lists or reference layout.
+int launch_exact_tc256(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s);
 
 // Process-wide options (fpx_set_option): which exact kernel the fused path runs, how many
 // of every 8 exp2 pairs the tcgen05 kernel computes on the FMA pipe (0, 2 or 3), which V1

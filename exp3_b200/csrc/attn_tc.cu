@@ -38,6 +38,7 @@
 #include <mutex>
 
 #include "attn.cuh"
+#include "softmax_tc.cuh"
 #include "tc.cuh"
 
 namespace fpx {
@@ -88,40 +89,6 @@ FPX_INLINE uint64_t desc_v(const uint8_t *tile, int kk) {
 FPX_INLINE uint32_t sw128_offset(int row, int col) {
   const int half = col >> 6, chunk = (col & 63) >> 3;
   return half * kHalf + row * 128 + ((chunk ^ (row & 7)) << 4) + ((col & 7) << 1);
-}
-
-// One 128-column row of P for a block: x = s * scale_log2 - m, p = 2^x, packed to bf16 into
-// TMEM (16 columns at a time); returns the row sum of p (fp32, before rounding, as the
-// reference's tile_denominator). kEmu of every 8 pairs use the FMA-pipe exp2.
-template <int kEmu>
-FPX_INLINE float softmax_row(const float (&sv)[128], float sl2, float neg, uint32_t p_addr) {
-  const uint64_t sl2x2 = pk2(sl2, sl2), negx2 = pk2(neg, neg);
-  uint64_t acc[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int q4 = 0; q4 < 4; ++q4) {
-    uint32_t pk[16];
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const uint64_t xx = ffma2(pk2(sv[32 * q4 + 2 * c], sv[32 * q4 + 2 * c + 1]), sl2x2, negx2);
-      uint64_t pp;
-      if ((c & 7) < kEmu) {
-        pp = exp2_poly2(xx);
-      } else {
-        float a, e;
-        up2(xx, a, e);
-        pp = pk2(ex2(a), ex2(e));
-      }
-      acc[c & 3] = fadd2(acc[c & 3], pp);
-      pk[c] = cvt_bf16x2(pp);
-    }
-    tmem_st16u(p_addr + 16 * q4, pk);
-  }
-  float a0, a1, a2, a3, b0, b1, b2, b3;
-  up2(acc[0], a0, b0);
-  up2(acc[1], a1, b1);
-  up2(acc[2], a2, b2);
-  up2(acc[3], a3, b3);
-  return ((a0 + b0) + (a1 + b1)) + ((a2 + b2) + (a3 + b3));
 }
 
 }  // namespace
@@ -470,12 +437,12 @@ EncodeTiledFn encode_fn() {
 
 }  // namespace
 
-// [B, rows, heads, 128] bf16 with element strides -> 4-D map (d, head, row, batch), box 64 x 1 x 128 x 1.
+// [B, rows, heads, d] bf16 with element strides -> 4-D map (d, head, row, batch), box 64 x 1 x box_rows x 1.
 bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int64_t rows, int64_t batch,
-               int64_t sh, int64_t sl, int64_t sb) {
+               int64_t sh, int64_t sl, int64_t sb, int box_rows) {
   cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)batch};
   cuuint64_t strides[3] = {(cuuint64_t)(sh * 2), (cuuint64_t)(sl * 2), (cuuint64_t)(sb * 2)};
-  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t box[4] = {64, 1, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   // A size-1 dimension may carry any stride; keep it a valid multiple of 16 bytes.
   if (heads == 1) strides[0] = 16;

@@ -1,0 +1,431 @@
+// Exact block-sparse causal attention at head dim 256 on the tcgen05 tensor core (the Qwen3.5
+// shape: 16 query heads over 4 KV heads, check_qwen35_math.py:93-185).
+//
+// Reference semantics are those of the d = 128 kernel (attn_tc.cu) and of
+// upstream/flashprefill_native_forward.py:215-354 with D_HEAD = 256: for query tile t of head h,
+// an online softmax in exp2 units over the tile's selected 128-key blocks in ascending order,
+// causal mask on the diagonal block, P rounded to bf16 before P.V, bf16 output, natural LSE.
+//
+// What changes with d = 256: a 128 x 256 fp32 accumulator takes 256 TMEM columns, so one CTA
+// runs ONE query tile (the G heads of a KV group run as neighbouring CTAs, which read the same
+// K/V blocks from L2), and double-buffers S instead:
+//   TMEM: S0 [0,128), S1 [128,256), O [256,512) fp32 columns x 128 lanes;
+//   P of block i (bf16, two per column) overwrites the first 64 columns of S(i & 1).
+// The tensor core computes QK^T of block i + 1 while the softmax works on block i:
+//   issue order  QK0, QK1, PV0, QK2, PV1, ..., QK(n-1), PV(n-2), PV(n-1).
+// Shared memory: Q (128 x 256 bf16, 64 KB, four 128-byte-swizzled 64-column atoms) and a ring
+// of five 32 KB stages, each holding 64 keys x 256 of K or of V, loaded in the order the tensor
+// core consumes them (K halves of block i + 1, then V halves of block i). 192 threads:
+//   warps 0..3  softmax (thread = query row = TMEM lane)
+//   warp 4      TMA producer (Q, then the K / V ring)       warp 5  MMA issuer, TMEM owner
+//
+// Ordering facts the protocol relies on: MMAs of one thread complete in issue order and a commit
+// tracks all earlier MMAs of the thread. So when s_full fires for block i, P(i-2).V has finished
+// (it was issued before QK(i)); the softmax only touches O when a row's max moves, and then
+// first waits for P(i-1).V on o_done[(i-1) & 1]. Two o_done barriers (one per parity of the
+// block) keep every wait within one phase of its barrier.
+//
+// Every wait is bounded (about 1 s); a wait that gives up flags the CTA and the device error
+// word, the roles drain their copies and MMAs in flight, and the CTA exits.
+#include <cuda.h>
+
+#include "attn.cuh"
+#include "softmax_tc.cuh"
+#include "tc.cuh"
+
+namespace fpx {
+namespace {
+
+using namespace tc;
+
+constexpr int kD = 256;
+constexpr uint32_t kQAtom = 128 * 128;     // 128 rows x 64 bf16: one 128-byte-swizzled atom column
+constexpr uint32_t kQBytes = 4 * kQAtom;   // 128 x 256 bf16
+constexpr uint32_t kKvAtom = 64 * 128;     // 64 rows x 64 bf16
+constexpr uint32_t kStageBytes = 4 * kKvAtom;  // 64 keys x 256 bf16
+constexpr int kStages = 5;
+constexpr int kThreads256 = 192;
+constexpr uint32_t kIdescQK = idesc_bf16(128, 64, false);
+constexpr uint32_t kIdescPV = idesc_bf16(128, 256, true);
+constexpr float kRescaleThreshold256 = 8.f;
+
+struct alignas(1024) Smem256 {
+  uint8_t q[kQBytes];  // Q; reused to stage the output tile
+  uint8_t ring[kStages][kStageBytes];
+  uint64_t q_full, full[kStages], empty[kStages], s_full[2], p_full[2], o_done[2], drain;
+  uint32_t tmem_base;
+  int abort, n, diag;
+};
+
+// K-major operands at K offset 16 * kk: 64-column atoms `atom` bytes apart, 32 B per K step
+// inside an atom, 8-row groups 1024 B apart.
+FPX_INLINE uint64_t desc_q256(const uint8_t *q, int kk) {
+  return smem_desc_sw128(smem_u32(q) + (kk >> 2) * kQAtom + (kk & 3) * 32, 16, 1024);
+}
+FPX_INLINE uint64_t desc_k256(const uint8_t *stage, int kk) {
+  return smem_desc_sw128(smem_u32(stage) + (kk >> 2) * kKvAtom + (kk & 3) * 32, 16, 1024);
+}
+// MN-major V (N = d) at key offset 16 * kk: 16 keys = 2048 B; the four 64-column MN atoms
+// kKvAtom apart; 8-key groups 1024 B apart.
+FPX_INLINE uint64_t desc_v256(const uint8_t *stage, int kk) {
+  return smem_desc_sw128(smem_u32(stage) + kk * 2048, kKvAtom, 1024);
+}
+// Byte offset of (row, col) in the 128 x 256 output tile (four swizzled 64-column atoms).
+FPX_INLINE uint32_t out_offset(int row, int col) {
+  const int atom = col >> 6, chunk = (col & 63) >> 3;
+  return atom * kQAtom + row * 128 + ((chunk ^ (row & 7)) << 4) + ((col & 7) << 1);
+}
+
+// Walks the valid entries of one tile's block list, 32 entries per step across the warp.
+// A trusted list (the fused path's own) takes every entry below its count; a reference-layout
+// list keeps entries with 0 <= blk <= t that are above the entry before them (the reference's
+// lists are ascending, so this drops the sentinel and anything past the tile).
+struct ListCursor {
+  const int32_t *lst;
+  const int64_t *ref;
+  int64_t ref_stride;
+  int cnt, t;
+  bool trusted;
+  int base, val, prev_last;
+  uint32_t mask;
+
+  FPX_INLINE void load(int lane) {
+    const int i = base + lane;
+    int v = -1;
+    if (i < cnt) v = ref ? (int)ref[(int64_t)i * ref_stride] : lst[i];
+    int prev = __shfl_up_sync(0xffffffffu, v, 1);
+    if (lane == 0) prev = prev_last;
+    const bool ok = i < cnt && (trusted || (v >= 0 && v <= t && v > prev));
+    val = v;
+    mask = __ballot_sync(0xffffffffu, ok);
+    prev_last = __shfl_sync(0xffffffffu, v, 31);
+  }
+  FPX_INLINE void start(int lane) {
+    base = 0;
+    prev_last = -1;
+    load(lane);
+  }
+  // Next valid block (warp-uniform), or -1 past the end.
+  FPX_INLINE int next(int lane) {
+    while (mask == 0u) {
+      base += 32;
+      if (base >= cnt) return -1;
+      load(lane);
+    }
+    const int bit = __ffs(mask) - 1;
+    mask &= mask - 1u;
+    return __shfl_sync(0xffffffffu, val, bit);
+  }
+};
+
+}  // namespace
+
+template <int kEmu>
+__global__ void __launch_bounds__(kThreads256, 1)
+    exact_tc256_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                       ExactParams p, int *err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  Smem256 &sh = *reinterpret_cast<Smem256 *>(smem_raw + pad);
+  volatile int *abort = &sh.abort;
+
+  const int G = p.group;
+  const int kv_local = blockIdx.z % p.kv_count;
+  const int b = blockIdx.z / p.kv_count;
+  const int kvh = p.head_begin / G + kv_local;
+  const int head = kvh * G + blockIdx.x;
+  const int t = p.tile_begin + (gridDim.y - 1 - blockIdx.y);  // longest tiles first
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool failed = err && *reinterpret_cast<volatile int *>(err) != 0;
+
+  const bool ref = p.ref_indices != nullptr;
+  const int nb = ref ? p.nb : p.route.nb;
+  ListCursor cur{};
+  if (ref) {
+    cur.ref = p.ref_indices + ((int64_t)b * nb + t) * nb * p.H + head;
+    cur.ref_stride = p.H;
+    cur.cnt = failed ? 0 : min(max(p.ref_counts[((int64_t)b * nb + t) * p.H + head], 0), nb);
+    cur.trusted = false;
+  } else {
+    const int64_t rr = p.route.row(b, head, t, p.H);
+    cur.lst = p.route.lists + rr * p.route.nb;
+    cur.cnt = failed ? 0 : min(max(p.route.counts[rr], 0), nb);
+    cur.trusted = true;
+  }
+  cur.t = t;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sh.q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&sh.s_full[x], 1);
+      mbar_init(&sh.p_full[x], 128);
+      mbar_init(&sh.o_done[x], 1);
+    }
+    mbar_init(&sh.drain, 1);
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {  // the tile's block count and whether its last block is the diagonal
+    int n = 0, last = -1;
+    if (cur.trusted) {
+      n = cur.cnt;
+      if (n > 0) last = cur.lst[n - 1];
+    } else {
+      cur.start(lane);
+      for (int blk = cur.next(lane); blk >= 0; blk = cur.next(lane)) {
+        ++n;
+        last = blk;
+      }
+    }
+    if (lane == 0) {
+      sh.n = n;
+      sh.diag = last == t;
+    }
+  }
+  if (warp == 5) {
+    tmem_alloc(&sh.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  const int n = sh.n;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer
+    if (n > 0) {
+      if (lane == 0) {
+        mbar_expect_tx(&sh.q_full, kQBytes);
+        for (int a = 0; a < 4; ++a) tma_load_4d(sh.q + a * kQAtom, &tm_q, &sh.q_full, 64 * a, head, t * 128, b);
+      }
+      int j = 0;
+      int issued[kStages] = {0, 0, 0, 0, 0};
+      bool ok = true;
+      // Two halves (64 keys each) of block blk's K or V into the next two ring stages.
+      auto load_block = [&](const CUtensorMap *map, int blk) {
+        for (int half = 0; half < 2 && ok; ++half, ++j) {
+          const int s = j % kStages, use = j / kStages;
+          if (use > 0 && !(ok = mbar_wait_warp(&sh.empty[s], (use - 1) & 1, abort))) break;
+          if (lane == 0) {
+            mbar_expect_tx(&sh.full[s], kStageBytes);
+            for (int a = 0; a < 4; ++a)
+              tma_load_4d(sh.ring[s] + a * kKvAtom, map, &sh.full[s], 64 * a, kvh, blk * 128 + 64 * half, b);
+          }
+          issued[s] = use + 1;
+        }
+      };
+      ListCursor kc = cur, vc = cur;
+      kc.start(lane);
+      vc.start(lane);
+      load_block(&tm_k, kc.next(lane));
+      for (int i = 0; i < n && ok; ++i) {
+        if (i + 1 < n) load_block(&tm_k, kc.next(lane));
+        load_block(&tm_v, vc.next(lane));
+      }
+      __syncwarp();
+      if (*abort) {  // drain copies still in flight before the shared memory goes away
+        int never = 0;
+        mbar_wait(&sh.q_full, 0, &never);
+        for (int s = 0; s < kStages; ++s)
+          if (issued[s] > 0) mbar_wait(&sh.full[s], (issued[s] - 1) & 1, &never);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (n > 0 && mbar_wait_warp(&sh.q_full, 0, abort)) {
+      int j = 0;
+      bool ok = true;
+      auto qk = [&](int i) {
+        const int buf = i & 1;
+        for (int half = 0; half < 2 && ok; ++half, ++j) {
+          const int s = j % kStages;
+          if (!(ok = mbar_wait_warp(&sh.full[s], (j / kStages) & 1, abort))) break;
+          tc_fence_after();
+          if (lane == 0) {
+#pragma unroll
+            for (int kk = 0; kk < kD / 16; ++kk)
+              mma_ss(tmem + 128 * buf + 64 * half, desc_q256(sh.q, kk), desc_k256(sh.ring[s], kk), kIdescQK,
+                     kk > 0 ? 1u : 0u);
+            tc_commit(&sh.empty[s]);
+          }
+          __syncwarp();
+        }
+        if (ok) {
+          if (lane == 0) tc_commit(&sh.s_full[buf]);
+          __syncwarp();
+        }
+      };
+      auto pv = [&](int i) {
+        const int buf = i & 1;
+        if (!(ok = mbar_wait_warp(&sh.p_full[buf], (i >> 1) & 1, abort))) return;
+        for (int half = 0; half < 2 && ok; ++half, ++j) {
+          const int s = j % kStages;
+          if (!(ok = mbar_wait_warp(&sh.full[s], (j / kStages) & 1, abort))) break;
+          tc_fence_after();
+          if (lane == 0) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_ts(tmem + 256, tmem + 128 * buf + 32 * half + 8 * kk, desc_v256(sh.ring[s], kk), kIdescPV,
+                     (i > 0 || half > 0 || kk > 0) ? 1u : 0u);
+            tc_commit(&sh.empty[s]);
+          }
+          __syncwarp();
+        }
+        if (ok) {
+          if (lane == 0) tc_commit(&sh.o_done[i & 1]);
+          __syncwarp();
+        }
+      };
+      qk(0);
+      for (int i = 0; i < n && ok; ++i) {
+        if (i + 1 < n) qk(i + 1);
+        if (ok) pv(i);
+      }
+      if (*abort) {  // let every MMA this thread issued finish before TMEM is released
+        int never = 0;
+        if (lane == 0) tc_commit(&sh.drain);
+        __syncwarp();
+        mbar_wait(&sh.drain, 0, &never);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax
+    const int r = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t o_addr = tmem + lane_off + 256;
+    const int qrow = t * 128 + r;
+    const float sl2 = p.scale_log2;
+    const bool last_is_diag = n > 0 && sh.diag;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int i = 0; i < n && ok; ++i) {
+      const int buf = i & 1;
+      const uint32_t s_addr = tmem + lane_off + 128 * buf;
+      if (!(ok = mbar_wait_warp(&sh.s_full[buf], (i >> 1) & 1, abort))) break;
+      tc_fence_after();
+      float sv[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, *reinterpret_cast<float(*)[32]>(&sv[32 * c]));
+      tmem_wait_ld();
+      const bool diag = last_is_diag && i == n - 1;
+      if (diag) {  // key j of the diagonal block is visible to row r iff j <= r
+#pragma unroll
+        for (int c = 0; c < 128; ++c) sv[c] = c <= r ? sv[c] : -INFINITY;
+      }
+      float mx[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mx[c] = sv[c];
+#pragma unroll
+      for (int c = 8; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+      const float bmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
+      const float mn = fmaxf(m, bmax);
+      float corr = 1.f;
+      // Each row decides for itself, as in the d = 128 kernel.
+      const bool move = mn > m + kRescaleThreshold256 || m == -INFINITY;
+      if (move) {
+        corr = (m == -INFINITY) ? 0.f : ex2(m - mn);
+        l *= corr;
+        m = mn;
+      }
+      const float neg = (m == -INFINITY) ? 0.f : -m;
+      l += diag ? softmax_row<0>(sv, sl2, neg, s_addr) : softmax_row<kEmu>(sv, sl2, neg, s_addr);
+      if (i > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+        // O must hold blocks < i before it is rescaled: wait for P(i-1).V.
+        if (!(ok = mbar_wait_warp(&sh.o_done[(i - 1) & 1], ((i - 1) >> 1) & 1, abort))) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float o[32];
+          tmem_ld32(o_addr + 32 * c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] *= corr;
+          tmem_st32(o_addr + 32 * c, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&sh.p_full[buf]);
+    }
+    // Epilogue: O / l -> bf16 -> swizzled tile (in the Q buffer) -> TMA store; LSE.
+    if (ok && n > 0 && !mbar_wait_warp(&sh.o_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort)) ok = false;
+    tc_fence_after();
+    const bool none = !(ok && n > 0) || m == -INFINITY;
+    const float inv = none ? 0.f : 1.f / l;
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      float o[32];
+      if (ok && n > 0) {
+        tmem_ld32(o_addr + 32 * c, o);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint4 v4 = make_uint4(pack_bf16(o[8 * e] * inv, o[8 * e + 1] * inv),
+                                    pack_bf16(o[8 * e + 2] * inv, o[8 * e + 3] * inv),
+                                    pack_bf16(o[8 * e + 4] * inv, o[8 * e + 5] * inv),
+                                    pack_bf16(o[8 * e + 6] * inv, o[8 * e + 7] * inv));
+        *reinterpret_cast<uint4 *>(sh.q + out_offset(r, 32 * c + 8 * e)) = v4;
+      }
+    }
+    if (p.lse && qrow < p.L) p.lse[((int64_t)b * p.L + qrow) * p.H + head] = none ? -INFINITY : m * kLn2 + logf(l);
+    fence_proxy_async();
+    named_sync(1, 128);
+    if (r == 0 && !*abort) {
+      for (int a = 0; a < 4; ++a) tma_store_4d(&tm_o, sh.q + a * kQAtom, 64 * a, head, t * 128, b);
+      bulk_commit();
+      bulk_wait0();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && sh.abort && err) atomicExch(err, 1);
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+namespace {
+template <int kEmu>
+void launch_variant256(dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap &tq, const CUtensorMap &tk,
+                       const CUtensorMap &tv, const CUtensorMap &to, const ExactParams &p, int *err) {
+  cudaFuncSetAttribute(exact_tc256_kernel<kEmu>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  exact_tc256_kernel<kEmu><<<grid, kThreads256, smem, s>>>(tq, tk, tv, to, p, err);
+}
+}  // namespace
+
+int launch_exact_tc256(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s) {
+  if (tiles <= 0 || heads <= 0) return FPX_OK;
+  if (p.group <= 0 || heads % p.group || p.head_begin % p.group) return FPX_ERR_SHAPE;
+  CUtensorMap tq, tk, tv, to;
+  if (!encode_4d(&tq, p.q, kD, p.H, L, B, p.q_sh, p.q_sl, p.q_sb, 128) ||
+      !encode_4d(&tk, p.k, kD, Hkv, L, B, p.k_sh, p.k_sl, p.k_sb, 64) ||
+      !encode_4d(&tv, p.v, kD, Hkv, L, B, p.v_sh, p.v_sl, p.v_sb, 64) ||
+      !encode_4d(&to, p.out, kD, p.H, L, B, p.o_sh, p.o_sl, p.o_sb, 128))
+    return FPX_ERR_INVALID;
+  ExactParams q = p;
+  q.kv_count = heads / p.group;
+  const dim3 grid(p.group, tiles, q.kv_count * B);
+  const size_t smem = sizeof(Smem256) + 1024;
+  int *err = device_error_word();
+  switch (get_option(kOptExpEmulation)) {
+    case 0: launch_variant256<0>(grid, smem, s, tq, tk, tv, to, q, err); break;
+    case 3: launch_variant256<3>(grid, smem, s, tq, tk, tv, to, q, err); break;
+    default: launch_variant256<2>(grid, smem, s, tq, tk, tv, to, q, err); break;
+  }
+  FPX_CHECK_LAUNCH();
+  return FPX_OK;
+}
+
+}  // namespace fpx

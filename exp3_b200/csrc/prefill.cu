@@ -22,7 +22,7 @@ struct Workspace {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-static Workspace carve(void *base, int B, int L, int H, int Hkv) {
+static Workspace carve(void *base, int B, int L, int H, int Hkv, int d = kHeadDim) {
   const int64_t nb = (L + kBlock - 1) / kBlock, words = (nb + 31) / 32;
   Workspace w{};
   size_t off = 0;
@@ -34,7 +34,7 @@ static Workspace carve(void *base, int B, int L, int H, int Hkv) {
   w.lists = reinterpret_cast<int32_t *>(take((size_t)B * H * nb * nb * 4));
   w.counts = reinterpret_cast<int32_t *>(take((size_t)B * H * nb * 4));
   w.tail = reinterpret_cast<uint32_t *>(take((size_t)B * H * nb * words * 4));
-  const size_t desc = (size_t)B * nb * Hkv * kHeadDim;
+  const size_t desc = (size_t)B * nb * Hkv * d;
   w.mk16 = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
   w.mkh = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
   w.mkl = reinterpret_cast<__nv_bfloat16 *>(take(desc * 2));
@@ -102,9 +102,9 @@ extern "C" int fpx_set_option(int key, int value) {
 
 extern "C" size_t fpx_prefill_workspace_bytes(int method, int B, int L, int H, int Hkv, int d,
                                               int block) {
-  (void)method; (void)d; (void)block;
-  if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0) return 0;
-  return carve(nullptr, B, L, H, Hkv).bytes;
+  (void)method; (void)block;
+  if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || (d != kHeadDim && d != 256)) return 0;
+  return carve(nullptr, B, L, H, Hkv, d).bytes;
 }
 
 extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int window, int last_full,
@@ -118,7 +118,10 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
                                      int stages, fpx_stream_t stream) {
   FPX_BIND(stream);
   if (method < 0 || method > FPX_METHOD_FP_V1_RESCUE_V2) return FPX_ERR_INVALID;
-  if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
+  if (block != kBlock) return FPX_ERR_UNSUPPORTED;
+  // Head dim 256 (the Qwen3.5 path, check_qwen35_math.py) runs dense and fp_v1.
+  if (d != kHeadDim && !(d == 256 && (method == FPX_METHOD_DENSE || method == FPX_METHOD_FP_V1)))
+    return FPX_ERR_UNSUPPORTED;
   if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
       !aligned16(out))
     return FPX_ERR_INVALID;
@@ -129,7 +132,7 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
   if (kv_begin < 0 || kv_end > Hkv || kv_begin >= kv_end || tile_begin < 0 || tile_end > nb ||
       tile_begin >= tile_end)
     return FPX_ERR_SHAPE;
-  const Workspace ws = carve(workspace, B, L, H, Hkv);
+  const Workspace ws = carve(workspace, B, L, H, Hkv, d);
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) || workspace_bytes < ws.bytes)
     return FPX_ERR_WORKSPACE;
   cudaStream_t s = stream;
@@ -155,6 +158,7 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     st.mean_bf16 = ws.mk16; st.mean_k = ws.mk; st.mean_v = ws.mv; st.var_k = ws.vk;
     st.sigma_v = ws.sv; st.counts = nullptr;
     st.mk_hi = ws.mkh; st.mk_lo = ws.mkl; st.mv_hi = ws.mvh; st.vk_hi = ws.vkh; st.vk_lo = ws.vkl;
+    st.d = d;
     if (method == FPX_METHOD_DENSE) {
       rc = launch_causal_route(rv, H, head_begin, heads, tile_begin, tiles, B, s);
     } else if (method == FPX_METHOD_FP_V1 || method == FPX_METHOD_MEAN_NATIVE || is_rescue_method(method)) {
@@ -166,7 +170,7 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
       vp.mean_k = ws.mk16; vp.L = L; vp.nb = nb; vp.H = H; vp.Hkv = Hkv; vp.group = G;
       vp.head_begin = head_begin; vp.tile_begin = tile_begin;
       vp.scale_log2 = (float)scale * kLog2e;
-      vp.scores = nullptr; vp.sel = sel;
+      vp.scores = nullptr; vp.sel = sel; vp.d = d;
       rc = launch_v1_route_selected(vp, tiles, heads, B, s);
     } else {
       rc = launch_block_stats(st, tile_end, kv_count, B, false, true, s);
@@ -199,9 +203,9 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     ep.head_begin = head_begin; ep.tile_begin = tile_begin;
     ep.scale_log2 = (float)scale * kLog2e;
     ep.route = rv;
-    rc = get_option(kOptExactKernel) == kExactKernelMmaSync
-             ? launch_exact_mma(ep, kExactLists, tiles, heads, B, s)
-             : launch_exact_tc(ep, B, L, Hkv, tiles, heads, s);
+    rc = d == 256 ? launch_exact_tc256(ep, B, L, Hkv, tiles, heads, s)
+         : get_option(kOptExactKernel) == kExactKernelMmaSync ? launch_exact_mma(ep, kExactLists, tiles, heads, B, s)
+                                                              : launch_exact_tc(ep, B, L, Hkv, tiles, heads, s);
     if (rc) return rc;
   }
   if ((stages & FPX_STAGE_MEAN) && is_mean_method(method)) {
@@ -243,9 +247,9 @@ extern "C" int fpx_prefill_export_routing(int method, int B, int L, int H, int H
                                           fpx_stream_t stream) {
   FPX_BIND(stream);
   (void)method;
-  if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
+  if ((d != kHeadDim && d != 256) || block != kBlock) return FPX_ERR_UNSUPPORTED;
   if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || (!selected && !indices)) return FPX_ERR_INVALID;
-  const Workspace ws = carve(const_cast<void *>(workspace), B, L, H, Hkv);
+  const Workspace ws = carve(const_cast<void *>(workspace), B, L, H, Hkv, d);
   if (!workspace || workspace_bytes < ws.bytes) return FPX_ERR_WORKSPACE;
   const int nb = (L + kBlock - 1) / kBlock;
   RouteView rv{ws.lists, ws.counts, ws.tail, nb, (nb + 31) / 32};
@@ -261,7 +265,7 @@ extern "C" int fpx_exact_attention(const void *q, int64_t q_sb, int64_t q_sl, in
                                    int H, int Hkv, int d, int block, double scale, void *out,
                                    float *lse, fpx_stream_t stream) {
   FPX_BIND(stream);
-  if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
+  if ((d != kHeadDim && d != 256) || block != kBlock) return FPX_ERR_UNSUPPORTED;
   if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
       !aligned16(out) || !indices || !counts || !lse)
     return FPX_ERR_INVALID;
@@ -277,11 +281,12 @@ extern "C" int fpx_exact_attention(const void *q, int64_t q_sb, int64_t q_sl, in
   ep.k_sb = k_sb; ep.k_sl = k_sl; ep.k_sh = k_sh;
   ep.v_sb = v_sb; ep.v_sl = v_sl; ep.v_sh = v_sh;
   ep.out = static_cast<__nv_bfloat16 *>(out);
-  ep.o_sb = (int64_t)L * H * kHeadDim; ep.o_sl = (int64_t)H * kHeadDim; ep.o_sh = kHeadDim;
+  ep.o_sb = (int64_t)L * H * d; ep.o_sl = (int64_t)H * d; ep.o_sh = d;
   ep.lse = lse; ep.L = L; ep.nb = nb; ep.H = H; ep.group = H / Hkv;
   ep.head_begin = 0; ep.tile_begin = 0;
   ep.scale_log2 = (float)scale * kLog2e;
   ep.ref_indices = indices; ep.ref_counts = counts;
+  if (d == 256) return launch_exact_tc256(ep, B, L, Hkv, nb, H, stream);
   return get_option(kOptExactKernel) == kExactKernelMmaSync ? launch_exact_mma(ep, kExactRefLayout, nb, H, B, stream)
                                                             : launch_exact_tc(ep, B, L, Hkv, nb, H, stream);
 }

@@ -16,8 +16,8 @@ namespace fpx {
 // walks the block's valid rows in order, so the fp32 sums have a fixed sequential order
 // (the bf16 V1 mean is bf16(sum / n), see upstream:58-68; the fp32 descriptors follow
 // kernels.py:22-46).
-template <bool kBf16Mean, bool kDesc>
-__global__ void __launch_bounds__(128) block_stats_kernel(StatsParams p) {
+template <bool kBf16Mean, bool kDesc, int D = kHeadDim>
+__global__ void __launch_bounds__(D) block_stats_kernel(StatsParams p) {
   const int blk = blockIdx.x, kvh = p.kv_begin + blockIdx.y, b = blockIdx.z;
   const int c = threadIdx.x;
   const int r0 = blk * kBlock;
@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(128) block_stats_kernel(StatsParams p) {
     }
   }
   const float fn = (float)n;
-  const int64_t o = (((int64_t)b * p.nb + blk) * p.Hkv + kvh) * kHeadDim + c;
+  const int64_t o = (((int64_t)b * p.nb + blk) * p.Hkv + kvh) * D + c;
   if (kBf16Mean) p.mean_bf16[o] = __float2bfloat16_rn(__fdiv_rn(sk, fn));
   if (kDesc) {
     __shared__ float red[4];
@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(128) block_stats_kernel(StatsParams p) {
       p.mv_hi[o] = __float2bfloat16_rn(mv);
     }
     const float var_v = fmaxf(__fsub_rn(__fdiv_rn(sv2, fn), __fmul_rn(mv, mv)), 0.f);
-    const float total = block_sum<128>(var_v, red);
+    const float total = block_sum<D>(var_v, red);
     if (c == 0) p.sigma_v[((int64_t)b * p.nb + blk) * p.Hkv + kvh] = sqrtf(total);
     if (p.counts && c == 0 && b == 0 && kvh == p.kv_begin) p.counts[blk] = n;
   }
@@ -69,6 +69,12 @@ int launch_block_stats(const StatsParams &p, int blocks, int kv_count, int B, bo
                        bool desc, cudaStream_t s) {
   if (blocks <= 0 || kv_count <= 0) return FPX_OK;
   dim3 grid(blocks, kv_count, B);
+  if (p.d == 256) {  // head dim 256: the V1 block mean only (fp_v1, check_qwen35_math.py:46-51)
+    if (desc || !bf16_mean) return FPX_ERR_UNSUPPORTED;
+    block_stats_kernel<true, false, 256><<<grid, 256, 0, s>>>(p);
+    FPX_CHECK_LAUNCH();
+    return FPX_OK;
+  }
   if (bf16_mean && desc)
     block_stats_kernel<true, true><<<grid, 128, 0, s>>>(p);
   else if (bf16_mean)
@@ -118,10 +124,13 @@ __device__ void select_and_emit(const float *sc, float smax, const SelectArgs &a
 // (upstream:410-417), then the threshold + protected selection (upstream:366-385).
 // 8 warps; warp w owns rows 16w..16w+15 of the tile. mean_k rows are staged 64 blocks at
 // a time; rows are padded to 136 bf16 so fragment loads hit 32 distinct banks.
-constexpr int kPad = 136;
 constexpr int kV1Chunk = 64;
 
+template <int D>
 __global__ void __launch_bounds__(256) v1_route_kernel(V1Params p) {
+  constexpr int kPad = D + 8;
+  constexpr int kChunks = D / 8;  // 16-byte pieces per row
+  constexpr int kSteps = D / 16;  // mma K steps
   const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);
   const int h = p.head_begin + blockIdx.y;
   const int b = blockIdx.z;
@@ -139,8 +148,8 @@ __global__ void __launch_bounds__(256) v1_route_kernel(V1Params p) {
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
   // Stage the query tile (zero rows past L).
-  for (int i = tid; i < kBlock * 16; i += 256) {
-    const int row = i >> 4, ch = i & 15;
+  for (int i = tid; i < kBlock * kChunks; i += 256) {
+    const int row = i / kChunks, ch = i % kChunks;
     const int pos = t * kBlock + row;
     uint4 val = make_uint4(0, 0, 0, 0);
     if (pos < p.L)
@@ -149,9 +158,9 @@ __global__ void __launch_bounds__(256) v1_route_kernel(V1Params p) {
     *reinterpret_cast<uint4 *>(sq + row * kPad + ch * 8) = val;
   }
   __syncthreads();
-  uint32_t af[8][4];
+  uint32_t af[kSteps][4];
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
+  for (int kk = 0; kk < kSteps; ++kk) {
     const __nv_bfloat16 *r0 = sq + (16 * warp + g) * kPad + 16 * kk + 2 * tq;
     const __nv_bfloat16 *r1 = r0 + 8 * kPad;
     af[kk][0] = *reinterpret_cast<const uint32_t *>(r0);
@@ -163,15 +172,15 @@ __global__ void __launch_bounds__(256) v1_route_kernel(V1Params p) {
   const int row_b = row_a + 8;
   const int last_row = t * kBlock + kBlock - 1;
   const int nblk = t + 1;
-  const __nv_bfloat16 *mk_base = p.mean_k + ((int64_t)b * p.nb * p.Hkv + kvh) * kHeadDim;
-  const int64_t mk_stride = (int64_t)p.Hkv * kHeadDim;
+  const __nv_bfloat16 *mk_base = p.mean_k + ((int64_t)b * p.nb * p.Hkv + kvh) * D;
+  const int64_t mk_stride = (int64_t)p.Hkv * D;
 
   for (int c0 = 0; c0 < nblk; c0 += kV1Chunk) {
     const int cn = min(kV1Chunk, nblk - c0);
     const int cn8 = (cn + 7) & ~7;
     __syncthreads();
-    for (int i = tid; i < cn8 * 16; i += 256) {
-      const int j = i >> 4, ch = i & 15;
+    for (int i = tid; i < cn8 * kChunks; i += 256) {
+      const int j = i / kChunks, ch = i % kChunks;
       uint4 val = make_uint4(0, 0, 0, 0);
       if (j < cn) val = *reinterpret_cast<const uint4 *>(mk_base + (c0 + j) * mk_stride + ch * 8);
       *reinterpret_cast<uint4 *>(smk + j * kPad + ch * 8) = val;
@@ -180,7 +189,7 @@ __global__ void __launch_bounds__(256) v1_route_kernel(V1Params p) {
     for (int j0 = 0; j0 < cn8; j0 += 8) {
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
+      for (int kk = 0; kk < kSteps; ++kk) {
         const __nv_bfloat16 *bp = smk + (j0 + g) * kPad + 16 * kk + 2 * tq;
         mma_bf16_16816(acc, af[kk], *reinterpret_cast<const uint32_t *>(bp),
                        *reinterpret_cast<const uint32_t *>(bp + 8));
@@ -249,21 +258,28 @@ __global__ void __launch_bounds__(256) v1_route_kernel(V1Params p) {
   if (p.sel.route.lists) select_and_emit<256, false>(sc, smax, p.sel, b, h, t, scratch);
 }
 
-size_t v1_route_smem(int nb) {
-  return (size_t)(kBlock + kV1Chunk) * kPad * 2 + 2 * 8 * kV1Chunk * 4 + 3 * (size_t)nb * 4 + 64;
+size_t v1_route_smem(int nb, int d) {
+  return (size_t)(kBlock + kV1Chunk) * (d + 8) * 2 + 2 * 8 * kV1Chunk * 4 + 3 * (size_t)nb * 4 + 64;
 }
 
 int launch_v1_route_selected(const V1Params &p, int tiles, int heads, int B, cudaStream_t s) {
-  return get_option(kOptRouteKernel) == kRouteKernelMmaSync ? launch_v1_route(p, tiles, heads, B, s)
-                                                            : launch_v1_route_tc(p, B, tiles, heads, s);
+  // The tcgen05 routing kernel is written for d = 128; head dim 256 takes the mma.sync one.
+  return (get_option(kOptRouteKernel) == kRouteKernelMmaSync || p.d == 256) ? launch_v1_route(p, tiles, heads, B, s)
+                                                                            : launch_v1_route_tc(p, B, tiles, heads, s);
 }
 
 int launch_v1_route(const V1Params &p, int tiles, int heads, int B, cudaStream_t s) {
   if (tiles <= 0 || heads <= 0) return FPX_OK;
-  const size_t smem = v1_route_smem(p.nb);
+  const int d = p.d == 256 ? 256 : kHeadDim;
+  const size_t smem = v1_route_smem(p.nb, d);
   if (smem > 200 * 1024) return FPX_ERR_UNSUPPORTED;
-  cudaFuncSetAttribute(v1_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  v1_route_kernel<<<dim3(tiles, heads, B), 256, smem, s>>>(p);
+  if (d == 256) {
+    cudaFuncSetAttribute(v1_route_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    v1_route_kernel<256><<<dim3(tiles, heads, B), 256, smem, s>>>(p);
+  } else {
+    cudaFuncSetAttribute(v1_route_kernel<kHeadDim>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    v1_route_kernel<kHeadDim><<<dim3(tiles, heads, B), 256, smem, s>>>(p);
+  }
   FPX_CHECK_LAUNCH();
   return FPX_OK;
 }
@@ -621,8 +637,9 @@ extern "C" int fpx_block_mean_k(const void *k, int64_t k_sb, int64_t k_sl, int64
                                 fpx_stream_t stream) {
   FPX_BIND(stream);
   if (!k || !mean_k || B <= 0 || L <= 0 || Hkv <= 0) return FPX_ERR_INVALID;
-  if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
+  if ((d != kHeadDim && d != 256) || block != kBlock) return FPX_ERR_UNSUPPORTED;
   StatsParams p{};
+  p.d = d;
   p.k = static_cast<const __nv_bfloat16 *>(k);
   p.k_sb = k_sb; p.k_sl = k_sl; p.k_sh = k_sh;
   p.v = p.k; p.v_sb = k_sb; p.v_sl = k_sl; p.v_sh = k_sh;
@@ -656,9 +673,10 @@ extern "C" int fpx_v1_scores(const void *q, int64_t q_sb, int64_t q_sl, int64_t 
   FPX_BIND(stream);
   if (!ptr_ok(q) || !ptr_ok(mean_k) || !scores || B <= 0 || L <= 0 || H <= 0 || Hkv <= 0)
     return FPX_ERR_INVALID;
-  if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
+  if ((d != kHeadDim && d != 256) || block != kBlock) return FPX_ERR_UNSUPPORTED;
   if (H % Hkv || !stride_ok(q_sb, q_sl, q_sh)) return FPX_ERR_SHAPE;
   V1Params p{};
+  p.d = d;
   p.q = static_cast<const __nv_bfloat16 *>(q);
   p.q_sb = q_sb; p.q_sl = q_sl; p.q_sh = q_sh;
   p.mean_k = static_cast<const __nv_bfloat16 *>(mean_k);

@@ -14,6 +14,7 @@ struct StatsParams {
   __nv_bfloat16 *mk_hi, *mk_lo, *mv_hi;          // bf16 splits for the tensor-core tail, or null
   __nv_bfloat16 *vk_hi, *vk_lo;                  // bf16 splits of var_k for the tensor-core selectors
   int32_t *counts;                               // [nb] or null
+  int d;                                         // head dim: 128 (0 reads as 128) or 256
 };
 
 // What the selection epilogue needs (compact lists are written when route.lists != null).
@@ -32,6 +33,7 @@ struct V1Params {
   float scale_log2;             // fp32(scale) * fp32(log2 e), as the reference kernel forms it
   float *scores;                // reference layout [B][nb][nb][H], or null
   SelectArgs sel;
+  int d;                        // head dim: 128 (0 reads as 128) or 256
 };
 
 struct SelParams {

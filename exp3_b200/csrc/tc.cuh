@@ -251,10 +251,10 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major)
 
 }  // namespace tc
 
-// [B, rows, heads, 128] bf16 with element strides -> 4-D TMA map (d, head, row, batch), box
-// 64 x 1 x 128 x 1, 128-byte swizzle, zero fill outside the tensor (attn_tc.cu).
+// [B, rows, heads, d] bf16 with element strides -> 4-D TMA map (d, head, row, batch), box
+// 64 x 1 x box_rows x 1, 128-byte swizzle, zero fill outside the tensor (attn_tc.cu).
 bool encode_4d(CUtensorMap *map, const void *base, int64_t d, int64_t heads, int64_t rows, int64_t batch,
-               int64_t sh, int64_t sl, int64_t sb);
+               int64_t sh, int64_t sl, int64_t sb, int box_rows = 128);
 
 // Device address of the library's error word (fpx_device_error) on the current device, for
 // kernels in other translation units; null if the runtime cannot resolve it.

@@ -164,6 +164,8 @@ class Qwen2Model:
         self.scale = cfg.head_dim ** -0.5
         self.k_cache = self.v_cache = None
         self.length = 0
+        self.peer_all_reduce = True
+        self._peer_ar = None
 
     # ---------------------------------------------------------------- pieces
     def _rmsnorm(self, x, weight, residual=None):
@@ -189,8 +191,18 @@ class Qwen2Model:
 
     def _all_reduce(self, t):
         if self.tp_size > 1:
-            torch.distributed.all_reduce(t, group=self.group)
+            if self._peer_ar is not None and self._peer_ar.fits(t):  # decode: one-shot over peer memory
+                self._peer_ar.all_reduce_(t)
+            else:
+                torch.distributed.all_reduce(t, group=self.group)
         return t
+
+    def _decode_comm(self):
+        """The decode step's small all-reduces go over NVLink peer memory (exp3_b200.comm) when
+        ``peer_all_reduce`` is set and the model is tensor parallel."""
+        if self.tp_size > 1 and self.peer_all_reduce and self._peer_ar is None:
+            from .comm import PeerAllReduce
+            self._peer_ar = PeerAllReduce(self.group, self.device, max_elems=8 * self.cfg.hidden_size)
 
     def _alloc_cache(self, capacity):
         shape = (self.cfg.num_hidden_layers, 1, capacity, len(self.kv), self.cfg.head_dim)
@@ -267,6 +279,7 @@ class Qwen2Model:
     @torch.inference_mode()
     def decode_step(self, token: torch.Tensor):
         """One dense greedy decode step (``evaluate.py:384-400``); returns the next token (device)."""
+        self._decode_comm()
         logits = self._forward(token.view(1), self.length, decoding=True)
         self.length += 1
         return logits.argmax()
@@ -287,6 +300,7 @@ class Qwen2Model:
         if steps == 1:
             return out
         cfg = self.cfg
+        self._decode_comm()
         need = int(lib().fpx_decode_workspace_bytes(1, 1, len(self.qh), len(self.kv), cap, cfg.head_dim))
         step = _GraphStep(
             pos32=torch.tensor([self.length], dtype=torch.int32, device=dev),

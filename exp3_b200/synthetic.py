@@ -32,12 +32,13 @@ class LayerShape:
     head_dim: int = 128
 
 
-# Benchmark configurations 1, 2, 4 and 5 (single attention layer shapes).
+# Benchmark configurations 1, 2, 4 and 5 (single attention layer shapes), and the head-dim-256 layer.
 CONFIGS = {
     "c1": (LayerShape(1, 4096, 28, 4), 8),
     "c2": (LayerShape(1, 32768, 28, 4), 32),
     "c4": (LayerShape(1, 131072, 28, 4), 128),
     "c5": (LayerShape(2, 65536, 40, 8), 0),
+    "q35": (LayerShape(1, 32768, 16, 4, 256), 32),  # head dim 256 (Qwen3.5-4B full-attention layers)
 }
 
 

@@ -170,6 +170,24 @@ int fpx_merge_exact_mean(const void *exact_out, const float *exact_lse, const fl
                          const float *mean_lse, int64_t rows, int d, void *out, float *lse,
                          fpx_stream_t stream);
 
+/* ---- one-shot all-reduce over NVLink peer memory (no reference counterpart) -------- */
+/* For the tensor-parallel decode step's small all-reduces. Each rank creates one buffer of
+ * fpx_ar_buffer_bytes(max_elems) (fpx_ar_create: cudaMalloc'd and zeroed, with its CUDA IPC
+ * handle, 64 bytes), the ranks exchange handles and map their peers' buffers (fpx_ar_open), and
+ * every rank then calls fpx_allreduce_bf16 with the world's buffer bases in rank order (its own
+ * at index rank). The sum is taken in rank order in fp32, so all ranks get the same bits; the
+ * call counter lives in the buffer, so calls can be captured in a CUDA graph. Waits for peers
+ * are bounded; a wait that gives up sets the buffer's error word (fpx_ar_error) and later calls
+ * return at once. Set-up allocates; the calls do not. */
+size_t fpx_ar_buffer_bytes(int max_elems);
+int fpx_ar_create(size_t bytes, void **base, void *ipc_handle);
+int fpx_ar_open(const void *ipc_handle, void **peer_base);
+int fpx_ar_close(void *peer_base);
+int fpx_ar_destroy(void *base);
+int fpx_ar_error(const void *base, int *code);
+int fpx_allreduce_bf16(void *inout, int64_t n, void *const *bases, int rank, int world, int max_elems,
+                       fpx_stream_t stream);
+
 /* ---- the fused prefill path (attention.py:210-333) ---------------------------------- */
 
 /* Device bytes of workspace fpx_prefill_attention needs (256-byte aligned). */

@@ -16,7 +16,10 @@ What runs, all on the CPU in fp32:
   helpers (``normalize_scores``, ``_deal_output_score_compiled``);
 - the fp32 restatements in ``check_math.py`` (``dense_reference``,
   ``v1_score_reference``, ``v1_selection_reference``,
-  ``explicit_mean_reference``, ``selector_reference``).
+  ``explicit_mean_reference``, ``selector_reference``);
+- for head dim 256 (the Qwen3.5 shape, 16 query heads over 4 KV heads), the same Triton
+  kernels with ``D_HEAD=256`` and the restatements in ``check_qwen35_math.py``
+  (``mean_reference``, ``score_reference``, ``selection_reference``, ``dense_reference``).
 
 The interpreter cannot run bf16 (it yields NaN), so bf16 inputs are upcast to
 fp32 first; values stay bf16-representable. Inputs are not stored: they are
@@ -50,8 +53,16 @@ def load_reference(root: str):
     return check_math, kernels, upstream
 
 
-def inputs(seed, length, heads, kv_heads):
-    shape = synthetic.LayerShape(1, length, heads, kv_heads)
+def load_qwen35(root: str):
+    """check_qwen35_math.py uses package-relative imports: import it as a package module."""
+    import importlib
+    parent, name = os.path.split(os.path.abspath(root))
+    sys.path.insert(0, parent)
+    return importlib.import_module(f"{name}.check_qwen35_math")
+
+
+def inputs(seed, length, heads, kv_heads, head_dim=128):
+    shape = synthetic.LayerShape(1, length, heads, kv_heads, head_dim)
     return synthetic.attention_inputs(shape, seed=seed, needles=2, apply_rope=True)
 
 
@@ -64,23 +75,23 @@ def ref_block_mean(upstream, k32):
     return mean
 
 
-def ref_v1_scores(upstream, q32, mk32):
+def ref_v1_scores(upstream, q32, mk32, scale=SCALE):
     b, length, h, d = q32.shape
     blocks, hkv = mk32.shape[1], mk32.shape[2]
     score = torch.full((b, blocks, blocks, h), float("-inf"))
     maximum = torch.full_like(score, float("-inf"))
     upstream.compute_block_score.fn[(blocks, b * h, 1)](
-        q32, mk32, SCALE, score, maximum, *q32.stride(), *mk32.stride(), *score.stride(),
+        q32, mk32, scale, score, maximum, *q32.stride(), *mk32.stride(), *score.stride(),
         *maximum.stride(), h, hkv, length, blocks, BLOCK_SIZE=128, K_TILE_SIZE=64, K_STRIDE=128, D_HEAD=d)
     return upstream.normalize_scores._torchdynamo_orig_callable(score, maximum)
 
 
-def ref_exact(upstream, q32, k32, v32, indices, counts):
+def ref_exact(upstream, q32, k32, v32, indices, counts, scale=SCALE):
     b, length, h, d = q32.shape
     out = torch.empty_like(q32)
     lse = torch.empty(b, length, h)
     upstream._flash_forward.fn[((length + 63) // 64, b * h, 1)](
-        q32, k32, v32, out, lse, indices, counts, SCALE, *q32.stride(), *k32.stride(), *v32.stride(),
+        q32, k32, v32, out, lse, indices, counts, scale, *q32.stride(), *k32.stride(), *v32.stride(),
         *out.stride(), *lse.stride(), *indices.stride(), *counts.stride(), length, length, h, k32.shape[2],
         Q_TILE_SIZE=64, K_TILE_SIZE=64, BLOCK_SIZE=128, D_HEAD=d)
     return out, lse
@@ -190,7 +201,58 @@ def main(root="/root/reference"):
         record[f"{name}_out_rows"] = o[:, ::9].numpy()
         record[f"{name}_lse"] = lse.numpy()
     np.savez_compressed(HERE / "rescue_l1153.npz", **record)
-    for name in ("v1_routing_l1089.npz", "exact_mean_l257.npz", "selectors_l385.npz", "rescue_l1153.npz"):
+
+    # Case 5: head dim 256, 16 query heads over 4 KV heads (check_qwen35_math.py:93-185): V1
+    # routing at L=1025 (9 blocks, the last with one row) and the exact path at L=385, all
+    # causal blocks and a fixed mask. O is stored on every 8th row of heads 0, 5, 10, 15.
+    q35 = load_qwen35(root)
+    scale256 = 256 ** -0.5
+    seed, length, heads, kv_heads = 35, 1025, 16, 4
+    q, k, v = inputs(seed, length, heads, kv_heads, 256)
+    q32, k32 = q.float(), k.float()
+    mean32 = ref_block_mean(upstream, k32)
+    torch.testing.assert_close(mean32, q35.mean_reference(k32), atol=1e-6, rtol=1e-6)
+    mk = mean32.to(torch.bfloat16)
+    scores = ref_v1_scores(upstream, q32, mk.float(), scale256)
+    # The reference's own gate (check_qwen35_math.py:117-124).
+    torch.testing.assert_close(scores, q35.score_reference(q32, mk.float(), scale256), atol=3e-4, rtol=0.008)
+    idx08, cnt08 = deal(upstream, scores, 0.08)
+    idx_p4, cnt_p4 = deal(upstream, scores.square().square(), 0.8)
+    ref_i, ref_c = q35.selection_reference(scores.square().square(), 0.8)
+    assert torch.equal(idx_p4, ref_i) and torch.equal(cnt_p4, ref_c)
+    record = {"seed": seed, "length": length, "heads": heads, "kv_heads": kv_heads, "head_dim": 256,
+              "digest": synthetic.tensor_digest(q, k, v),
+              "block_mean_fp32": mean32.numpy(), "mean_k_bf16_bits": mk.view(torch.int16).numpy(),
+              "scores": scores.numpy(), "indices_a008": idx08.numpy(), "counts_a008": cnt08.numpy(),
+              "indices_pow4_a08": idx_p4.numpy(), "counts_pow4_a08": cnt_p4.numpy()}
+    np.savez_compressed(HERE / "qwen35_routing_l1025.npz", **record)
+    seed, length = 36, 385
+    q, k, v = inputs(seed, length, heads, kv_heads, 256)
+    q32, k32, v32 = q.float(), k.float(), v.float()
+    blocks = 4
+    all_selected = kernels.protected_selection(torch.zeros(1, blocks, blocks, heads), 0.0, 2, 4, 2)
+    a_idx, a_cnt = kernels.indices_from_mask(all_selected)
+    out_all, lse_all = ref_exact(upstream, q32, k32, v32, a_idx, a_cnt, scale256)
+    dense_o, dense_lse = q35.dense_reference(q32, k32, v32, scale256)
+    torch.testing.assert_close(out_all, dense_o, atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(lse_all, dense_lse, atol=1e-5, rtol=1e-5)
+    selected = all_selected.clone()
+    selected[:, 3, 1, ::2] = False
+    selected[:, 3, 0, 1::4] = False
+    selected[:, 2, 0, 3::4] = False
+    f_idx, f_cnt = kernels.indices_from_mask(selected)
+    out_fixed, lse_fixed = ref_exact(upstream, q32, k32, v32, f_idx, f_cnt, scale256)
+    keep_heads = [0, 5, 10, 15]
+    np.savez_compressed(
+        HERE / "qwen35_exact_l385.npz",
+        seed=seed, length=length, heads=heads, kv_heads=kv_heads, head_dim=256,
+        digest=synthetic.tensor_digest(q, k, v), rows=np.arange(0, length, 8), out_heads=np.array(keep_heads),
+        lse_all=lse_all.numpy(), out_all_rows=out_all[:, ::8][:, :, keep_heads].numpy(),
+        selected_fixed=selected.numpy(), indices_fixed=f_idx.numpy(), counts_fixed=f_cnt.numpy(),
+        lse_fixed=lse_fixed.numpy(), out_fixed_rows=out_fixed[:, ::8][:, :, keep_heads].numpy(),
+    )
+    for name in ("v1_routing_l1089.npz", "exact_mean_l257.npz", "selectors_l385.npz", "rescue_l1153.npz",
+                 "qwen35_routing_l1025.npz", "qwen35_exact_l385.npz"):
         print(name, (HERE / name).stat().st_size, "bytes")
 
 

@@ -14,7 +14,8 @@ SCALE = 128 ** -0.5
 def load(name):
     """Returns (fixture dict, q, k, v) with bf16 inputs checked against the stored digest."""
     data = dict(np.load(GOLDEN / name, allow_pickle=False))
-    shape = synthetic.LayerShape(1, int(data["length"]), int(data["heads"]), int(data["kv_heads"]))
+    shape = synthetic.LayerShape(1, int(data["length"]), int(data["heads"]), int(data["kv_heads"]),
+                                 int(data.get("head_dim", 128)))
     q, k, v = synthetic.attention_inputs(shape, seed=int(data["seed"]), needles=2, apply_rope=True)
     digest = synthetic.tensor_digest(q, k, v)
     assert digest == str(data["digest"]), (

@@ -1,0 +1,119 @@
+"""Head dim 256 (the Qwen3.5 shape: 16 query heads over 4 KV heads, check_qwen35_math.py:93-185).
+
+The reference's fp_v1 path at d = 256 through the C ABI: the bf16 block mean, the V1 scores and
+selection against the reference's golden vectors, the tcgen05 d = 256 exact kernel in the
+reference layout (all causal blocks, and a fixed mask), and the fused fp_v1 / dense prefill
+against the oracle. Bars as for d = 128: masks bit-exact outside the 1e-6 band, O 2e-2, LSE 1e-3.
+"""
+
+import pytest
+import torch
+
+import oracle
+from exp3_b200 import _capi, ops, synthetic, upstream
+from exp3_b200.attention import AttentionBackend
+from golden_cases import load, t
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+SCALE = 256 ** -0.5
+O_TOL, LSE_TOL, BAND = 2e-2, 1e-3, 1e-6
+
+
+def test_block_mean_and_scores_match_reference():
+    data, q, k, v = load("qwen35_routing_l1025.npz")
+    mine = upstream.block_mean_k(k.to(DEV)).cpu()
+    assert torch.equal(mine.view(torch.int16), oracle.block_mean_k(k).view(torch.int16))
+    torch.testing.assert_close(mine.float(), t(data["block_mean_fp32"]), atol=2e-3, rtol=2e-2)
+    mk = t(data["mean_k_bf16_bits"]).view(torch.bfloat16)
+    scores = upstream.v1_scores(q.to(DEV), mk.to(DEV), SCALE).cpu()
+    torch.testing.assert_close(scores, t(data["scores"]), atol=1e-6, rtol=1e-5)
+    idx, cnt = upstream.deal_output_score(t(data["scores"]).to(DEV).square().square(), 2, 4, 0.8, 2, 0)
+    assert torch.equal(idx.cpu(), t(data["indices_pow4_a08"])) and torch.equal(cnt.cpu(), t(data["counts_pow4_a08"]))
+
+
+def test_exact_attention_matches_reference():
+    data, q, k, v = load("qwen35_exact_l385.npz")
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    rows, heads = t(data["rows"]), t(data["out_heads"])
+    for tag in ("fixed", "all"):
+        if tag == "fixed":
+            idx, cnt = t(data["indices_fixed"]), t(data["counts_fixed"])
+        else:
+            idx, cnt = oracle.indices_from_mask(oracle.protected_selection(torch.zeros(1, 4, 4, 16), 0.0, 2, 4, 2))
+        out, lse = upstream.exact_attention(qd, kd, vd, idx.to(DEV), cnt.to(DEV), SCALE)
+        assert out.shape == (1, 385, 16, 256)
+        torch.testing.assert_close(lse.cpu(), t(data[f"lse_{tag}"]), atol=LSE_TOL, rtol=0)
+        torch.testing.assert_close(out.cpu().float()[:, rows][:, :, heads], t(data[f"out_{tag}_rows"]),
+                                   atol=O_TOL, rtol=0)
+        # every row and head against the oracle
+        o_ref, l_ref = oracle.exact_attention(q.float(), k.float(), v.float(), idx, cnt, SCALE)
+        torch.testing.assert_close(out.cpu().float(), o_ref, atol=O_TOL, rtol=0)
+    assert _capi.device_error() == 0
+
+
+def _fused_vs_oracle(method, q, k, v, alpha, tiles):
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    batch, length, heads, d = q.shape
+    lse = torch.empty(batch, length, heads, device=DEV)
+    out = ops.prefill_attention(qd, kd, vd, method, alpha, SCALE, lse=lse)
+    sel, _, cnt = ops.export_routing(method, batch, length, heads, k.shape[2], head_dim=d)
+    sel = sel.cpu()
+    outs, ref_sel, ref_scores = oracle.prefill_attention_tiles(method, q, k, v, SCALE, alpha, tiles=tiles)
+    compared = 0
+    for tile in tiles:
+        diff = sel[:, tile] != ref_sel[:, tile]
+        if diff.any():
+            s = ref_scores[:, tile]
+            band = (s - s.amax(dim=1, keepdim=True) * alpha).abs() <= BAND
+            assert bool((diff <= band).all()), f"{method}: mask differs outside the band on tile {tile}"
+            continue
+        lo, hi = 128 * tile, min(length, 128 * tile + 128)
+        o_ref, l_ref = outs[tile]
+        torch.testing.assert_close(out[:, lo:hi].cpu().float(), o_ref.float(), atol=O_TOL, rtol=0)
+        torch.testing.assert_close(lse[:, lo:hi].cpu(), l_ref, atol=LSE_TOL, rtol=0)
+        compared += 1
+    assert compared >= len(tiles) // 2
+    return sel
+
+
+@pytest.mark.parametrize("method", ["fp_v1", "dense"])
+def test_fused_prefill_head_dim_256(method):
+    shape = synthetic.LayerShape(1, 2177, 16, 4, 256)  # 18 blocks, the last with one row
+    q, k, v = synthetic.attention_inputs(shape, seed=41, needles=4, structured_sigma=0.5)
+    blocks = oracle.num_blocks(2177)
+    sel = _fused_vs_oracle(method, q, k, v, 0.08, list(range(blocks)))
+    if method == "fp_v1":
+        assert int(sel.sum()) < 16 * blocks * (blocks + 1) // 2  # structured inputs route blocks away
+
+
+def test_fused_prefill_head_dim_256_batch_and_edges():
+    for length in (1, 129, 385):
+        shape = synthetic.LayerShape(2, length, 8, 2, 256)
+        q, k, v = synthetic.attention_inputs(shape, seed=length, needles=1)
+        _fused_vs_oracle("fp_v1", q, k, v, 0.08, list(range(oracle.num_blocks(length))))
+
+
+def test_backend_fp_v1_at_head_dim_256():
+    """The reference's own gate (check_qwen35_math.py:153-168): the backend at alpha 0 equals dense."""
+    shape = synthetic.LayerShape(1, 257, 16, 4, 256)
+    q, k, v = synthetic.attention_inputs(shape, seed=35)
+    backend = AttentionBackend(alpha=0.0)
+    backend.configure("fp_v1", 0.0)
+
+    class Layer:
+        layer_idx = 3
+
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    out, _ = backend.forward(Layer(), qd.transpose(1, 2).contiguous(), kd.transpose(1, 2).contiguous(),
+                             vd.transpose(1, 2).contiguous(), None, SCALE)
+    tiles = oracle.dense_attention(q.float(), k.float(), v.float(), SCALE)
+    ref = torch.cat([tiles[i][0] for i in sorted(tiles)], dim=1)
+    torch.testing.assert_close(out.cpu().float(), ref, atol=0.03, rtol=0.03)
+
+
+def test_mean_methods_refuse_head_dim_256():
+    shape = synthetic.LayerShape(1, 256, 4, 1, 256)
+    q, k, v = (x.to(DEV) for x in synthetic.attention_inputs(shape, seed=1))
+    with pytest.raises(RuntimeError):
+        ops.prefill_attention(q, k, v, "mean_native", 0.08, SCALE)

@@ -116,3 +116,37 @@ def test_rescue_tails_match_reference():
         out, lse = oracle.rescue_tail(q, k, v, selected, SCALE, remainder=remainder)
         torch.testing.assert_close(lse, t(data[f"{name}_lse"]), atol=1e-5, rtol=1e-5)
         torch.testing.assert_close(out[:, rows], t(data[f"{name}_out_rows"]), atol=1e-5, rtol=1e-5)
+
+
+# ---------------------------------------------------------------- head dim 256 (Qwen3.5 shape)
+
+
+def test_head_dim_256_routing_matches_reference():
+    data, q, k, v = load("qwen35_routing_l1025.npz")
+    assert q.shape == (1, 1025, 16, 256) and k.shape == (1, 1025, 4, 256)
+    mine = oracle.block_mean_k(k)
+    ref = t(data["block_mean_fp32"])
+    torch.testing.assert_close(mine.float(), ref, atol=2e-3, rtol=2e-2)
+    assert (mine == ref.to(torch.bfloat16)).float().mean().item() > 0.999
+    mk = t(data["mean_k_bf16_bits"]).view(torch.bfloat16)
+    scores = oracle.v1_scores(q, mk, 256 ** -0.5)
+    torch.testing.assert_close(scores, t(data["scores"]), atol=1e-6, rtol=1e-5)
+    ref_scores = t(data["scores"])
+    idx, cnt = oracle.deal_output_score(ref_scores, 2, 4, 0.08, 2, 0)
+    assert torch.equal(idx, t(data["indices_a008"])) and torch.equal(cnt, t(data["counts_a008"]))
+    idx, cnt = oracle.deal_output_score(ref_scores.square().square(), 2, 4, 0.8, 2, 0)
+    assert torch.equal(idx, t(data["indices_pow4_a08"])) and torch.equal(cnt, t(data["counts_pow4_a08"]))
+
+
+def test_head_dim_256_exact_path_matches_reference():
+    data, q, k, v = load("qwen35_exact_l385.npz")
+    q32, k32, v32 = q.float(), k.float(), v.float()
+    rows, heads = t(data["rows"]), t(data["out_heads"])
+    out, lse = oracle.exact_attention(q32, k32, v32, t(data["indices_fixed"]), t(data["counts_fixed"]), 256 ** -0.5)
+    torch.testing.assert_close(lse, t(data["lse_fixed"]), atol=2e-6, rtol=1e-5)
+    torch.testing.assert_close(out[:, rows][:, :, heads], t(data["out_fixed_rows"]), atol=2e-6, rtol=1e-5)
+    every = oracle.protected_selection(torch.zeros(1, 4, 4, 16), 0.0, 2, 4, 2)
+    idx, cnt = oracle.indices_from_mask(every)
+    out, lse = oracle.exact_attention(q32, k32, v32, idx, cnt, 256 ** -0.5)
+    torch.testing.assert_close(lse, t(data["lse_all"]), atol=2e-6, rtol=1e-5)
+    torch.testing.assert_close(out[:, rows][:, :, heads], t(data["out_all_rows"]), atol=2e-6, rtol=1e-5)
