@@ -340,6 +340,11 @@ def run_model(args, rank, world, local):
     # the graph run includes its one eager warm-up step and the capture.
     decode_eager_ms = timed(decode_eager, 1) / max(1, args.decode_tokens - 1)
     decode_ms = timed(decode_graph, 1) / max(1, args.decode_tokens - 1)
+    replay_ms = model.replay_ms_per_token()
+    if world > 1 and replay_ms is not None:
+        t = torch.tensor([replay_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        replay_ms = float(t)
     # End to end (evaluate.prefill): token ids from pinned host memory, prefill, first token to host.
     result = torch.empty(1, dtype=torch.int64).pin_memory()
 
@@ -360,12 +365,18 @@ def run_model(args, rank, world, local):
                            "parallelism": f"tp{world} (heads / FFN sharded, NCCL all-reduce after o_proj and down)",
                            "prefill_tflops_dense_equivalent": flops / (prefill_ms * 1e-3) / 1e12,
                            "decode_ms_per_token": decode_ms, "decode_ms_per_token_eager": decode_eager_ms,
-                           "decode": "CUDA-graph steps (Model.decode_graph)", "decode_tokens": args.decode_tokens},
+                           "decode_replay_ms_per_token": replay_ms,
+                           "decode": "CUDA-graph steps (Model.decode_graph); decode_ms_per_token includes the "
+                                     "eager warm-up step and the capture, decode_replay_ms_per_token is the "
+                                     "steady-state replay",
+                           "decode_comm": "one-shot peer-memory all-reduce (exp3_b200.comm)" if world > 1 else None,
+                           "decode_tokens": args.decode_tokens},
                 "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": ids_host.numel() * 8,
                         "d2h_bytes_per_step": 8},
                 "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
     if world > 1:
+        model.close_comm()
         dist.barrier()
         dist.destroy_process_group()
 

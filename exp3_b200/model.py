@@ -160,12 +160,24 @@ class Qwen2Model:
                 lw.full = None
             self.layers.append(lw)
         self.norm = torch.ones(cfg.hidden_size, dtype=torch.bfloat16, device=self.device)
-        self.lm_head = _Init(seed + 7, self.device).normal((cfg.vocab_size, cfg.hidden_size), cfg.initializer_range)
+        lm_head = _Init(seed + 7, self.device).normal((cfg.vocab_size, cfg.hidden_size), cfg.initializer_range)
+        # Vocab-sharded LM head under tensor parallelism: each rank holds vocab / N rows and the
+        # last token's logits are all-gathered (the head is 1.09 GB: replicated, it would be
+        # read in full by every rank at every decode step).
+        if tp_size > 1 and cfg.vocab_size % tp_size == 0:
+            rows = cfg.vocab_size // tp_size
+            self.lm_head = lm_head[tp_rank * rows:(tp_rank + 1) * rows].contiguous()
+            self.vocab_sharded = True
+        else:
+            self.lm_head = lm_head
+            self.vocab_sharded = False
+        del lm_head
         self.scale = cfg.head_dim ** -0.5
         self.k_cache = self.v_cache = None
         self.length = 0
         self.peer_all_reduce = True
         self._peer_ar = None
+        self.replay_events = None  # (start, end, replays) of the last decode_graph
 
     # ---------------------------------------------------------------- pieces
     def _rmsnorm(self, x, weight, residual=None):
@@ -261,6 +273,10 @@ class Qwen2Model:
             h, down = self._layer(i, h, x, pos0, length, decoding, step)
         last = self._rmsnorm(down[-1:].contiguous(), self.norm, residual=h[-1:].contiguous())
         logits = (last @ self.lm_head.t()).float()  # bf16 LM head, as HF's lm_head
+        if self.vocab_sharded:
+            full = torch.empty(self.tp_size * logits.shape[-1], dtype=logits.dtype, device=logits.device)
+            torch.distributed.all_gather_into_tensor(full, logits.view(-1), group=self.group)
+            return full
         return logits[-1]
 
     # ---------------------------------------------------------------- public
@@ -325,9 +341,13 @@ class Qwen2Model:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             one_step()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
         for i in range(2, steps):
             graph.replay()
             out[i] = step.token[0]
+        end.record()
+        self.replay_events = (start, end, steps - 2)
         del graph  # a graph holding NCCL calls must go before the process group
         self.length += steps - 1
         return out
@@ -340,6 +360,24 @@ class Qwen2Model:
             token = self.decode_step(token)
             out.append(token)
         return torch.stack(out)
+
+    def close_comm(self):
+        """Unmaps the peer all-reduce buffers (every rank calls it; no kernel of theirs may be
+        in flight, hence the synchronize and barrier first)."""
+        if self._peer_ar is not None:
+            torch.cuda.synchronize(self.device)
+            torch.distributed.barrier(group=self.group)
+            self._peer_ar.close()
+            self._peer_ar = None
+
+    def replay_ms_per_token(self) -> float | None:
+        """Device time per step of the last ``decode_graph``'s replays (after its eager warm-up
+        step and the capture), or None."""
+        if not self.replay_events or self.replay_events[2] <= 0:
+            return None
+        start, end, n = self.replay_events
+        end.synchronize()
+        return start.elapsed_time(end) / n
 
     def prefill_flops(self, length: int, exact_pairs: int | None = None) -> float:
         """Algorithmic FLOPs of one prefill: 2 x params x L for the linear layers (last-token LM

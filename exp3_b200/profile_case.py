@@ -1,6 +1,6 @@
 """Runs the fused prefill attention layer a few times on one shape: the command profiled by ncu.
 
-    python -m exp3_b200.profile_case [--length 32768] [--method mean_native] [--alpha 0.08]
+    python -m exp3_b200.profile_case [--length 32768] [--head-dim 128|256] [--method mean_native] [--alpha 0.08]
                                      [--repeats 3] [--variant iid|structured] [--kernel tcgen05]
 
 Exits 0 after printing per-stage CUDA-event times of the last repeat; it is meant to be run
@@ -22,6 +22,7 @@ def main():
     ap.add_argument("--length", type=int, default=32768)
     ap.add_argument("--heads", type=int, default=28)
     ap.add_argument("--kv-heads", type=int, default=4)
+    ap.add_argument("--head-dim", type=int, default=128, choices=[128, 256])
     ap.add_argument("--method", default="mean_native")
     ap.add_argument("--alpha", type=float, default=0.08)
     ap.add_argument("--repeats", type=int, default=3)
@@ -30,13 +31,13 @@ def main():
     ap.add_argument("--emulate", type=int, default=0, choices=[0, 2, 3])
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
-    shape = synthetic.LayerShape(1, args.length, args.heads, args.kv_heads)
+    shape = synthetic.LayerShape(1, args.length, args.heads, args.kv_heads, args.head_dim)
     q, k, v = synthetic.attention_inputs(shape, seed=0, needles=32, device=dev,
                                          structured_sigma=0.5 if args.variant == "structured" else 0.0)
     _capi.set_exact_kernel(args.kernel)
     _capi.set_exp_emulation(args.emulate)
     out = torch.empty_like(q)
-    scale = 128 ** -0.5
+    scale = args.head_dim ** -0.5
     times = {}
     for _ in range(args.repeats):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
