@@ -73,6 +73,8 @@ def parse():
     ap.add_argument("--alpha", type=float, default=0.08)
     ap.add_argument("--variant", default="iid", choices=["iid", "structured"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exact-kernel", default="tcgen05", choices=["tcgen05", "tcgen05_single", "mma"],
+                    help="exact-attention kernel at head dim 128 (head dim 256 always runs tcgen05_single)")
     ap.add_argument("--config", default="c2", choices=sorted(LAYER_CONFIGS),
                     help="layer workload: c2 (32K, the headline), c4 (128K), c5 (32B shape, B=2, 64K), "
                          "q35 (head dim 256, 32K)")
@@ -403,6 +405,8 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from exp3_b200 import _capi
+    _capi.set_exact_kernel(args.exact_kernel)
     cfg = LAYER_CONFIGS[args.config]
     b, length, heads, kv_heads, d = cfg["batch"], cfg["length"], cfg["heads"], cfg["kv_heads"], cfg.get("head_dim", 128)
     scale = d ** -0.5
@@ -563,7 +567,7 @@ def main():
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": cfg["workload"], "method": method, "alpha": alpha, "variant": args.variant,
-                       "ms_per_layer": ms_step, "density": density, "exact_token_pairs": all_pairs,
+                       "exact_kernel": "tcgen05_single" if d == 256 else args.exact_kernel, "ms_per_layer": ms_step, "density": density, "exact_token_pairs": all_pairs,
                        "l2": f"no flush: Q ({q.numel() * 2 / 1e6:.0f} MB) and O are larger than the 126 MB L2",
                        "parallelism": f"{world} rank(s): (KV group x query-tile range) shards, no collective",
                        "stage_ms_rank0": {"route": route_ms, "exact": exact_ms, "mean_merge": mean_ms}},

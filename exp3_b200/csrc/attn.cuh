@@ -24,15 +24,16 @@ struct ExactParams {
 int launch_exact_mma(const ExactParams &p, int mode, int tiles, int heads, int B, cudaStream_t s);
 // tcgen05 / TMEM / TMA exact kernel over internal lists (kExactLists).
 int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s);
-// Head dim 256 (attn_tc256.cu): one query tile per CTA, lists or reference layout.
-int launch_exact_tc256(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s);
+// One query tile per CTA with double-buffered S (attn_tc1.cu), head dim d = 128 or 256, lists
+// or reference layout.
+int launch_exact_tc1(const ExactParams &p, int d, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s);
 
 // Process-wide options (fpx_set_option): which exact kernel the fused path runs, how many
 // of every 8 exp2 pairs the tcgen05 kernel computes on the FMA pipe (0, 2 or 3), which V1
 // routing kernel, mean-tail kernel and new-selector routing kernel run.
 enum Option { kOptExactKernel = 1, kOptExpEmulation = 2, kOptRouteKernel = 3, kOptMeanKernel = 4,
               kOptSelectorKernel = 5 };
-enum ExactKernel { kExactKernelTcgen05 = 0, kExactKernelMmaSync = 1 };
+enum ExactKernel { kExactKernelTcgen05 = 0, kExactKernelMmaSync = 1, kExactKernelTcgen05Single = 2 };
 enum RouteKernel { kRouteKernelTcgen05 = 0, kRouteKernelMmaSync = 1 };
 enum MeanKernel { kMeanKernelTcgen05 = 0, kMeanKernelFp32 = 1 };
 enum SelectorKernel { kSelectorKernelTcgen05 = 0, kSelectorKernelFp32 = 1 };

@@ -1,21 +1,23 @@
-// Exact block-sparse causal attention at head dim 256 on the tcgen05 tensor core (the Qwen3.5
-// shape: 16 query heads over 4 KV heads, check_qwen35_math.py:93-185).
+// Exact block-sparse causal attention, one query tile per CTA, on the tcgen05 tensor core, for
+// head dim D = 128 and D = 256 (the Qwen3.5 shape: 16 query heads over 4 KV heads,
+// check_qwen35_math.py:93-185).
 //
-// Reference semantics are those of the d = 128 kernel (attn_tc.cu) and of
-// upstream/flashprefill_native_forward.py:215-354 with D_HEAD = 256: for query tile t of head h,
-// an online softmax in exp2 units over the tile's selected 128-key blocks in ascending order,
-// causal mask on the diagonal block, P rounded to bf16 before P.V, bf16 output, natural LSE.
+// Reference semantics are those of upstream/flashprefill_native_forward.py:215-354 (and of the
+// two-tile kernel in attn_tc.cu): for query tile t of head h, an online softmax in exp2 units
+// over the tile's selected 128-key blocks in ascending order, causal mask on the diagonal
+// block, P rounded to bf16 before P.V, bf16 output, natural LSE.
 //
-// What changes with d = 256: a 128 x 256 fp32 accumulator takes 256 TMEM columns, so one CTA
-// runs ONE query tile (the G heads of a KV group run as neighbouring CTAs, which read the same
-// K/V blocks from L2), and double-buffers S instead:
-//   TMEM: S0 [0,128), S1 [128,256), O [256,512) fp32 columns x 128 lanes;
+// One CTA runs ONE query tile (the G heads of a KV group run as neighbouring CTAs, which read
+// the same K/V blocks from L2) and double-buffers S, so the softmax never waits for the tensor
+// core to turn P(i) into S(i + 1):
+//   TMEM: S0 [0,128), S1 [128,256), O [256,256+D) fp32 columns x 128 lanes;
 //   P of block i (bf16, two per column) overwrites the first 64 columns of S(i & 1).
 // The tensor core computes QK^T of block i + 1 while the softmax works on block i:
 //   issue order  QK0, QK1, PV0, QK2, PV1, ..., QK(n-1), PV(n-2), PV(n-1).
-// Shared memory: Q (128 x 256 bf16, 64 KB, four 128-byte-swizzled 64-column atoms) and a ring
-// of five 32 KB stages, each holding 64 keys x 256 of K or of V, loaded in the order the tensor
-// core consumes them (K halves of block i + 1, then V halves of block i). 192 threads:
+// Shared memory: Q (128 x D bf16, D/64 128-byte-swizzled 64-column atoms) and a ring of
+// stages, each holding 64 keys x D of K or of V, loaded in the order the tensor core consumes
+// them (K halves of block i + 1, then V halves of block i): twelve 16 KB stages at D = 128,
+// five 32 KB stages at D = 256 (Q + ring = 224 KB either way). 192 threads:
 //   warps 0..3  softmax (thread = query row = TMEM lane)
 //   warp 4      TMA producer (Q, then the K / V ring)       warp 5  MMA issuer, TMEM owner
 //
@@ -38,39 +40,44 @@ namespace {
 
 using namespace tc;
 
-constexpr int kD = 256;
-constexpr uint32_t kQAtom = 128 * 128;     // 128 rows x 64 bf16: one 128-byte-swizzled atom column
-constexpr uint32_t kQBytes = 4 * kQAtom;   // 128 x 256 bf16
-constexpr uint32_t kKvAtom = 64 * 128;     // 64 rows x 64 bf16
-constexpr uint32_t kStageBytes = 4 * kKvAtom;  // 64 keys x 256 bf16
-constexpr int kStages = 5;
-constexpr int kThreads256 = 192;
+constexpr uint32_t kQAtom = 128 * 128;  // 128 rows x 64 bf16: one 128-byte-swizzled atom column
+constexpr uint32_t kKvAtom = 64 * 128;  // 64 rows x 64 bf16
+constexpr int kThreads1 = 192;
 constexpr uint32_t kIdescQK = idesc_bf16(128, 64, false);
-constexpr uint32_t kIdescPV = idesc_bf16(128, 256, true);
-constexpr float kRescaleThreshold256 = 8.f;
+constexpr float kRescaleThreshold1 = 8.f;
 
-struct alignas(1024) Smem256 {
-  uint8_t q[kQBytes];  // Q; reused to stage the output tile
-  uint8_t ring[kStages][kStageBytes];
-  uint64_t q_full, full[kStages], empty[kStages], s_full[2], p_full[2], o_done[2], drain;
+template <int D>
+struct Geometry {
+  static constexpr int kAtoms = D / 64;
+  static constexpr uint32_t kQBytes = kAtoms * kQAtom;       // 128 x D bf16
+  static constexpr uint32_t kStageBytes = kAtoms * kKvAtom;  // 64 keys x D bf16
+  static constexpr int kStages = D == 128 ? 12 : 5;
+  static constexpr uint32_t kIdescPV = idesc_bf16(128, D, true);
+};
+
+template <int D>
+struct alignas(1024) Smem1 {
+  uint8_t q[Geometry<D>::kQBytes];  // Q; reused to stage the output tile
+  uint8_t ring[Geometry<D>::kStages][Geometry<D>::kStageBytes];
+  uint64_t q_full, full[Geometry<D>::kStages], empty[Geometry<D>::kStages], s_full[2], p_full[2], o_done[2], drain;
   uint32_t tmem_base;
   int abort, n, diag;
 };
 
 // K-major operands at K offset 16 * kk: 64-column atoms `atom` bytes apart, 32 B per K step
 // inside an atom, 8-row groups 1024 B apart.
-FPX_INLINE uint64_t desc_q256(const uint8_t *q, int kk) {
+FPX_INLINE uint64_t desc_q1(const uint8_t *q, int kk) {
   return smem_desc_sw128(smem_u32(q) + (kk >> 2) * kQAtom + (kk & 3) * 32, 16, 1024);
 }
-FPX_INLINE uint64_t desc_k256(const uint8_t *stage, int kk) {
+FPX_INLINE uint64_t desc_k1(const uint8_t *stage, int kk) {
   return smem_desc_sw128(smem_u32(stage) + (kk >> 2) * kKvAtom + (kk & 3) * 32, 16, 1024);
 }
-// MN-major V (N = d) at key offset 16 * kk: 16 keys = 2048 B; the four 64-column MN atoms
-// kKvAtom apart; 8-key groups 1024 B apart.
-FPX_INLINE uint64_t desc_v256(const uint8_t *stage, int kk) {
+// MN-major V (N = D) at key offset 16 * kk: 16 keys = 2048 B; the 64-column MN atoms kKvAtom
+// apart; 8-key groups 1024 B apart.
+FPX_INLINE uint64_t desc_v1(const uint8_t *stage, int kk) {
   return smem_desc_sw128(smem_u32(stage) + kk * 2048, kKvAtom, 1024);
 }
-// Byte offset of (row, col) in the 128 x 256 output tile (four swizzled 64-column atoms).
+// Byte offset of (row, col) in the 128 x D output tile (swizzled 64-column atoms).
 FPX_INLINE uint32_t out_offset(int row, int col) {
   const int atom = col >> 6, chunk = (col & 63) >> 3;
   return atom * kQAtom + row * 128 + ((chunk ^ (row & 7)) << 4) + ((col & 7) << 1);
@@ -120,14 +127,17 @@ struct ListCursor {
 
 }  // namespace
 
-template <int kEmu>
-__global__ void __launch_bounds__(kThreads256, 1)
-    exact_tc256_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                       ExactParams p, int *err) {
+template <int D, int kEmu>
+__global__ void __launch_bounds__(kThreads1, 1)
+    exact_tc1_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                     ExactParams p, int *err) {
+  using Geo = Geometry<D>;
+  constexpr int kStages = Geo::kStages;
+  constexpr int kAtoms = Geo::kAtoms;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  Smem256 &sh = *reinterpret_cast<Smem256 *>(smem_raw + pad);
+  Smem1<D> &sh = *reinterpret_cast<Smem1<D> *>(smem_raw + pad);
   volatile int *abort = &sh.abort;
 
   const int G = p.group;
@@ -201,11 +211,13 @@ __global__ void __launch_bounds__(kThreads256, 1)
     // ---------------------------------------------------------------- TMA producer
     if (n > 0) {
       if (lane == 0) {
-        mbar_expect_tx(&sh.q_full, kQBytes);
-        for (int a = 0; a < 4; ++a) tma_load_4d(sh.q + a * kQAtom, &tm_q, &sh.q_full, 64 * a, head, t * 128, b);
+        mbar_expect_tx(&sh.q_full, Geo::kQBytes);
+        for (int a = 0; a < kAtoms; ++a) tma_load_4d(sh.q + a * kQAtom, &tm_q, &sh.q_full, 64 * a, head, t * 128, b);
       }
       int j = 0;
-      int issued[kStages] = {0, 0, 0, 0, 0};
+      int issued[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) issued[s] = 0;
       bool ok = true;
       // Two halves (64 keys each) of block blk's K or V into the next two ring stages.
       auto load_block = [&](const CUtensorMap *map, int blk) {
@@ -213,8 +225,8 @@ __global__ void __launch_bounds__(kThreads256, 1)
           const int s = j % kStages, use = j / kStages;
           if (use > 0 && !(ok = mbar_wait_warp(&sh.empty[s], (use - 1) & 1, abort))) break;
           if (lane == 0) {
-            mbar_expect_tx(&sh.full[s], kStageBytes);
-            for (int a = 0; a < 4; ++a)
+            mbar_expect_tx(&sh.full[s], Geo::kStageBytes);
+            for (int a = 0; a < kAtoms; ++a)
               tma_load_4d(sh.ring[s] + a * kKvAtom, map, &sh.full[s], 64 * a, kvh, blk * 128 + 64 * half, b);
           }
           issued[s] = use + 1;
@@ -249,8 +261,8 @@ __global__ void __launch_bounds__(kThreads256, 1)
           tc_fence_after();
           if (lane == 0) {
 #pragma unroll
-            for (int kk = 0; kk < kD / 16; ++kk)
-              mma_ss(tmem + 128 * buf + 64 * half, desc_q256(sh.q, kk), desc_k256(sh.ring[s], kk), kIdescQK,
+            for (int kk = 0; kk < D / 16; ++kk)
+              mma_ss(tmem + 128 * buf + 64 * half, desc_q1(sh.q, kk), desc_k1(sh.ring[s], kk), kIdescQK,
                      kk > 0 ? 1u : 0u);
             tc_commit(&sh.empty[s]);
           }
@@ -271,7 +283,7 @@ __global__ void __launch_bounds__(kThreads256, 1)
           if (lane == 0) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              mma_ts(tmem + 256, tmem + 128 * buf + 32 * half + 8 * kk, desc_v256(sh.ring[s], kk), kIdescPV,
+              mma_ts(tmem + 256, tmem + 128 * buf + 32 * half + 8 * kk, desc_v1(sh.ring[s], kk), Geo::kIdescPV,
                      (i > 0 || half > 0 || kk > 0) ? 1u : 0u);
             tc_commit(&sh.empty[s]);
           }
@@ -328,7 +340,7 @@ __global__ void __launch_bounds__(kThreads256, 1)
       const float mn = fmaxf(m, bmax);
       float corr = 1.f;
       // Each row decides for itself, as in the d = 128 kernel.
-      const bool move = mn > m + kRescaleThreshold256 || m == -INFINITY;
+      const bool move = mn > m + kRescaleThreshold1 || m == -INFINITY;
       if (move) {
         corr = (m == -INFINITY) ? 0.f : ex2(m - mn);
         l *= corr;
@@ -341,7 +353,7 @@ __global__ void __launch_bounds__(kThreads256, 1)
         if (!(ok = mbar_wait_warp(&sh.o_done[(i - 1) & 1], ((i - 1) >> 1) & 1, abort))) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < D / 32; ++c) {
           float o[32];
           tmem_ld32(o_addr + 32 * c, o);
           tmem_wait_ld();
@@ -360,7 +372,7 @@ __global__ void __launch_bounds__(kThreads256, 1)
     const bool none = !(ok && n > 0) || m == -INFINITY;
     const float inv = none ? 0.f : 1.f / l;
 #pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < D / 32; ++c) {
       float o[32];
       if (ok && n > 0) {
         tmem_ld32(o_addr + 32 * c, o);
@@ -382,7 +394,7 @@ __global__ void __launch_bounds__(kThreads256, 1)
     fence_proxy_async();
     named_sync(1, 128);
     if (r == 0 && !*abort) {
-      for (int a = 0; a < 4; ++a) tma_store_4d(&tm_o, sh.q + a * kQAtom, 64 * a, head, t * 128, b);
+      for (int a = 0; a < kAtoms; ++a) tma_store_4d(&tm_o, sh.q + a * kQAtom, 64 * a, head, t * 128, b);
       bulk_commit();
       bulk_wait0();
     }
@@ -397,33 +409,43 @@ __global__ void __launch_bounds__(kThreads256, 1)
 }
 
 namespace {
-template <int kEmu>
-void launch_variant256(dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap &tq, const CUtensorMap &tk,
-                       const CUtensorMap &tv, const CUtensorMap &to, const ExactParams &p, int *err) {
-  cudaFuncSetAttribute(exact_tc256_kernel<kEmu>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  exact_tc256_kernel<kEmu><<<grid, kThreads256, smem, s>>>(tq, tk, tv, to, p, err);
+template <int D, int kEmu>
+void launch_variant1(dim3 grid, cudaStream_t s, const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
+                     const CUtensorMap &to, const ExactParams &p, int *err) {
+  const size_t smem = sizeof(Smem1<D>) + 1024;
+  cudaFuncSetAttribute(exact_tc1_kernel<D, kEmu>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  exact_tc1_kernel<D, kEmu><<<grid, kThreads1, smem, s>>>(tq, tk, tv, to, p, err);
+}
+
+template <int D>
+void launch_d(dim3 grid, cudaStream_t s, const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
+              const CUtensorMap &to, const ExactParams &p, int *err) {
+  switch (get_option(kOptExpEmulation)) {
+    case 0: launch_variant1<D, 0>(grid, s, tq, tk, tv, to, p, err); break;
+    case 3: launch_variant1<D, 3>(grid, s, tq, tk, tv, to, p, err); break;
+    default: launch_variant1<D, 2>(grid, s, tq, tk, tv, to, p, err); break;
+  }
 }
 }  // namespace
 
-int launch_exact_tc256(const ExactParams &p, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s) {
+int launch_exact_tc1(const ExactParams &p, int d, int B, int L, int Hkv, int tiles, int heads, cudaStream_t s) {
   if (tiles <= 0 || heads <= 0) return FPX_OK;
+  if (d != 128 && d != 256) return FPX_ERR_UNSUPPORTED;
   if (p.group <= 0 || heads % p.group || p.head_begin % p.group) return FPX_ERR_SHAPE;
   CUtensorMap tq, tk, tv, to;
-  if (!encode_4d(&tq, p.q, kD, p.H, L, B, p.q_sh, p.q_sl, p.q_sb, 128) ||
-      !encode_4d(&tk, p.k, kD, Hkv, L, B, p.k_sh, p.k_sl, p.k_sb, 64) ||
-      !encode_4d(&tv, p.v, kD, Hkv, L, B, p.v_sh, p.v_sl, p.v_sb, 64) ||
-      !encode_4d(&to, p.out, kD, p.H, L, B, p.o_sh, p.o_sl, p.o_sb, 128))
+  if (!encode_4d(&tq, p.q, d, p.H, L, B, p.q_sh, p.q_sl, p.q_sb, 128) ||
+      !encode_4d(&tk, p.k, d, Hkv, L, B, p.k_sh, p.k_sl, p.k_sb, 64) ||
+      !encode_4d(&tv, p.v, d, Hkv, L, B, p.v_sh, p.v_sl, p.v_sb, 64) ||
+      !encode_4d(&to, p.out, d, p.H, L, B, p.o_sh, p.o_sl, p.o_sb, 128))
     return FPX_ERR_INVALID;
   ExactParams q = p;
   q.kv_count = heads / p.group;
   const dim3 grid(p.group, tiles, q.kv_count * B);
-  const size_t smem = sizeof(Smem256) + 1024;
   int *err = device_error_word();
-  switch (get_option(kOptExpEmulation)) {
-    case 0: launch_variant256<0>(grid, smem, s, tq, tk, tv, to, q, err); break;
-    case 3: launch_variant256<3>(grid, smem, s, tq, tk, tv, to, q, err); break;
-    default: launch_variant256<2>(grid, smem, s, tq, tk, tv, to, q, err); break;
-  }
+  if (d == 128)
+    launch_d<128>(grid, s, tq, tk, tv, to, q, err);
+  else
+    launch_d<256>(grid, s, tq, tk, tv, to, q, err);
   FPX_CHECK_LAUNCH();
   return FPX_OK;
 }

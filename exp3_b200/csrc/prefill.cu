@@ -89,7 +89,8 @@ int get_option(int key) { return (key > 0 && key < 6) ? g_options[key] : 0; }
 }  // namespace fpx
 
 extern "C" int fpx_set_option(int key, int value) {
-  if ((key == kOptExactKernel && (value == kExactKernelTcgen05 || value == kExactKernelMmaSync)) ||
+  if ((key == kOptExactKernel && (value == kExactKernelTcgen05 || value == kExactKernelMmaSync ||
+                                  value == kExactKernelTcgen05Single)) ||
       (key == kOptExpEmulation && (value == 0 || value == 2 || value == 3)) ||
       (key == kOptRouteKernel && (value == kRouteKernelTcgen05 || value == kRouteKernelMmaSync)) ||
       (key == kOptMeanKernel && (value == kMeanKernelTcgen05 || value == kMeanKernelFp32)) ||
@@ -203,9 +204,10 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     ep.head_begin = head_begin; ep.tile_begin = tile_begin;
     ep.scale_log2 = (float)scale * kLog2e;
     ep.route = rv;
-    rc = d == 256 ? launch_exact_tc256(ep, B, L, Hkv, tiles, heads, s)
-         : get_option(kOptExactKernel) == kExactKernelMmaSync ? launch_exact_mma(ep, kExactLists, tiles, heads, B, s)
-                                                              : launch_exact_tc(ep, B, L, Hkv, tiles, heads, s);
+    const int ek = get_option(kOptExactKernel);
+    rc = (d == 256 || ek == kExactKernelTcgen05Single) ? launch_exact_tc1(ep, d, B, L, Hkv, tiles, heads, s)
+         : ek == kExactKernelMmaSync ? launch_exact_mma(ep, kExactLists, tiles, heads, B, s)
+                                     : launch_exact_tc(ep, B, L, Hkv, tiles, heads, s);
     if (rc) return rc;
   }
   if ((stages & FPX_STAGE_MEAN) && is_mean_method(method)) {
@@ -286,7 +288,8 @@ extern "C" int fpx_exact_attention(const void *q, int64_t q_sb, int64_t q_sl, in
   ep.head_begin = 0; ep.tile_begin = 0;
   ep.scale_log2 = (float)scale * kLog2e;
   ep.ref_indices = indices; ep.ref_counts = counts;
-  if (d == 256) return launch_exact_tc256(ep, B, L, Hkv, nb, H, stream);
+  if (d == 256 || get_option(kOptExactKernel) == kExactKernelTcgen05Single)
+    return launch_exact_tc1(ep, d, B, L, Hkv, nb, H, stream);
   return get_option(kOptExactKernel) == kExactKernelMmaSync ? launch_exact_mma(ep, kExactRefLayout, nb, H, B, stream)
                                                             : launch_exact_tc(ep, B, L, Hkv, nb, H, stream);
 }

@@ -1,5 +1,5 @@
-// The softmax step shared by the tcgen05 exact kernels (attn_tc.cu, attn_tc256.cu): one thread
-// owns one query row (one TMEM lane) of a 128-key block.
+// The softmax step shared by the tcgen05 exact kernels (attn_tc.cu, attn_tc1.cu, attn_tc2.cu):
+// one thread owns one query row (one TMEM lane) of a block of NC keys (128, or a 64-key half).
 #pragma once
 
 #include "tc.cuh"
@@ -7,15 +7,15 @@
 namespace fpx {
 namespace tc {
 
-// One 128-column row of P for a block: x = s * scale_log2 - m, p = 2^x, packed to bf16 into
-// TMEM (16 columns at a time); returns the row sum of p (fp32, before rounding, as the
-// reference's tile_denominator). kEmu of every 8 pairs use the FMA-pipe exp2.
-template <int kEmu>
-FPX_INLINE float softmax_row(const float (&sv)[128], float sl2, float neg, uint32_t p_addr) {
+// One NC-column row of P: x = s * scale_log2 - m, p = 2^x, packed to bf16 into TMEM (16
+// columns at a time); returns the row sum of p (fp32, before rounding, as the reference's
+// tile_denominator). kEmu of every 8 pairs use the FMA-pipe exp2.
+template <int kEmu, int NC = 128>
+FPX_INLINE float softmax_row(const float (&sv)[NC], float sl2, float neg, uint32_t p_addr) {
   const uint64_t sl2x2 = pk2(sl2, sl2), negx2 = pk2(neg, neg);
   uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int q4 = 0; q4 < 4; ++q4) {
+  for (int q4 = 0; q4 < NC / 32; ++q4) {
     uint32_t pk[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c) {

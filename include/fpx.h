@@ -65,8 +65,9 @@ const char *fpx_status_string(int status);
 int fpx_version(void);
 
 /* Process-wide options (no reference counterpart). Key 1 selects the exact-attention kernel of
- * fpx_prefill_attention: 0 = tcgen05/TMEM/TMA, two query tiles per CTA (default), 1 = mma.sync
- * (cross-check). Key 2 sets how many of every 8 exp2 pairs the tcgen05 kernel evaluates with
+ * fpx_prefill_attention and fpx_exact_attention at head dim 128: 0 = tcgen05/TMEM/TMA, two
+ * query tiles per CTA (default), 1 = mma.sync (cross-check), 2 = tcgen05, one query tile per
+ * CTA with double-buffered S (the kernel head dim 256 always uses). Key 2 sets how many of every 8 exp2 pairs the tcgen05 kernel evaluates with
  * an FMA-pipe polynomial instead of the special-function unit: 0 (default), 2 or 3. Key 3
  * selects the V1 routing kernel (fpx_prefill_attention and fpx_v1_scores): 0 = tcgen05,
  * transposed block-mean x Q products in TMEM (default), 1 = mma.sync (cross-check). Key 4

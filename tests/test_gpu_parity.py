@@ -317,6 +317,43 @@ def test_tcgen05_and_mma_exact_kernels_agree():
     assert _capi.device_error() == 0
 
 
+@pytest.mark.parametrize("method", ["mean_native", "fp_v1", "dense", "cgf_mean"])
+def test_single_tile_exact_kernel_matches_oracle(method):
+    """The one-tile-per-CTA tcgen05 kernel (double-buffered S) at head dim 128, selected with
+    fpx_set_option(1, 2): the fused path against the oracle, ragged last tile, B = 2."""
+    shape = synthetic.LayerShape(2, 2177, 14, 2)
+    q, k, v = synthetic.attention_inputs(shape, seed=12, needles=4, structured_sigma=0.5)
+    try:
+        _capi.set_exact_kernel("tcgen05_single")
+        run_fused_vs_oracle(method, q, k, v, 0.08, list(range(oracle.num_blocks(2177))))
+    finally:
+        _capi.set_exact_kernel("tcgen05")
+    assert _capi.device_error() == 0
+
+
+def test_single_tile_exact_kernel_reference_layout_and_agreement():
+    data, q, k, v = load("exact_mean_l257.npz")
+    qd, kd, vd = cuda(q, k, v)
+    idx, cnt = t(data["indices_fixed"]).to(DEV), t(data["counts_fixed"]).to(DEV)
+    shape = synthetic.LayerShape(1, 32768, 28, 4)
+    q2, k2, v2 = cuda(*synthetic.attention_inputs(shape, seed=8, needles=8, structured_sigma=0.5))
+    results = []
+    try:
+        for which in ("tcgen05_single", "tcgen05"):
+            _capi.set_exact_kernel(which)
+            out, lse = upstream.exact_attention(qd, kd, vd, idx, cnt, SCALE)
+            torch.testing.assert_close(out.cpu().float(), t(data["out_fixed"]), atol=O_TOL, rtol=0)
+            torch.testing.assert_close(lse.cpu(), t(data["lse_fixed"]), atol=LSE_TOL, rtol=0)
+            lse2 = torch.empty(1, 32768, 28, device=DEV)
+            results.append((ops.prefill_attention(q2, k2, v2, "mean_native", 0.08, SCALE, lse=lse2), lse2))
+    finally:
+        _capi.set_exact_kernel("tcgen05")
+    # 32K: the two tcgen05 kernels agree (same products, same rounding points)
+    torch.testing.assert_close(results[0][0].float(), results[1][0].float(), atol=O_TOL, rtol=0)
+    torch.testing.assert_close(results[0][1], results[1][1], atol=LSE_TOL, rtol=0)
+    assert _capi.device_error() == 0
+
+
 @pytest.mark.parametrize("length,heads,kv", [(2049, 14, 2), (32768, 28, 4), (40000, 10, 2), (65600, 4, 2)])
 def test_tcgen05_and_mma_route_kernels_agree(length, heads, kv):
     """The tensor-core V1 routing (transposed products in TMEM, persistent CTAs) against the
