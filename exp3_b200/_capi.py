@@ -153,8 +153,8 @@ def set_route_kernel(name: str) -> None:
 
 
 def set_mean_kernel(name: str) -> None:
-    """Selects the fused path's mean-tail kernel: "tcgen05" (the default) or "fp32" (the
-    CUDA-core cross-check)."""
+    """Selects the fused path's tail kernels (block-mean and rescue tails): "tcgen05" (the
+    default) or "fp32" (the CUDA-core cross-check)."""
     call("fpx_set_option", 4, {"tcgen05": 0, "fp32": 1}[name])
 
 

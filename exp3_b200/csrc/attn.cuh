@@ -69,6 +69,9 @@ int launch_mean_tail(const MeanParams &p, int mode, int tiles, int heads, int B,
 // Rescue token of every tail block (kernels.py:276-285) into p.choice; the tail comes from the
 // route's bits (kMeanMergeInPlace) or from the mask (kMeanStandalone).
 int launch_rescue_choice(const MeanParams &p, int mode, int tiles, int kv_count, int B, cudaStream_t s);
+// Rescue tails (keys 1 / 2) on the tensor core, merged in place (rescue_tc.cu); needs choice,
+// k, v, mean_k, mean_v, route (tail bits), out and lse.
+int launch_rescue_tail_tc(const MeanParams &p, int keys, int B, int L, int tiles, int heads, cudaStream_t s);
 // tcgen05 / TMEM / TMA tail, merged in place (attn_tail_tc.cu); needs mk_hi, mk_lo, mv_hi.
 int launch_mean_tail_tc(const MeanParams &p, int B, int tiles, int heads, cudaStream_t s);
 int launch_merge(const __nv_bfloat16 *exact_out, const float *exact_lse, const float *mean_out,

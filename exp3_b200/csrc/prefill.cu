@@ -237,8 +237,9 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     mp.lse = lse_out;
     rc = launch_rescue_choice(mp, kMeanMergeInPlace, tiles, kv_count, B, s);
     if (rc) return rc;
-    rc = launch_mean_tail(mp, kMeanMergeInPlace, tiles, heads, B, s,
-                          method == FPX_METHOD_FP_V1_RESCUE_V2 ? 2 : 1);
+    const int keys = method == FPX_METHOD_FP_V1_RESCUE_V2 ? 2 : 1;
+    rc = get_option(kOptMeanKernel) == kMeanKernelFp32 ? launch_mean_tail(mp, kMeanMergeInPlace, tiles, heads, B, s, keys)
+                                                       : launch_rescue_tail_tc(mp, keys, B, L, tiles, heads, s);
   }
   return rc;
 }

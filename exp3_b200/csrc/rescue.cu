@@ -5,30 +5,38 @@
 // (torch.argmax: the first maximum on ties). The tail tokens then enter the rescue tail through
 // mean_tail_kernel (mean.cu).
 //
-// One CTA per (b, KV group, t), 128 threads. The group's query means are formed in shared
-// memory (thread = dimension; the rows are summed in order, then divided by the row count).
-// For every block in the union of the group's tails, thread j loads token j's key row into
-// registers and forms one dot product per head with the broadcast means; a (value, index)
+// kRescueSplits CTAs per (b, KV group, t), 256 threads each. Every CTA forms the group's query
+// means in shared memory (fp32 sums of the valid rows, then divided by the row count) and
+// compacts the union of the group's tails into a list; CTA s of the split takes list entries
+// s, s + kRescueSplits, ... For each of its blocks, thread pair (2j, 2j + 1) holds token j's key
+// row in registers, 64 dimensions each (the next block's row is loaded while the current one is
+// reduced), and forms one dot product per head with the broadcast means; a (value, index)
 // maximum over the 128 tokens gives each head's choice.
 #include "attn.cuh"
 
 namespace fpx {
 
 constexpr int kRescueMaxGroup = 16;
+constexpr int kRescueSplits = 4;
+constexpr int kChoiceThreads = 256;
 
 template <int kMode>
-__global__ void __launch_bounds__(128) rescue_choice_kernel(MeanParams p) {
+__global__ void __launch_bounds__(256, 2) rescue_choice_kernel(MeanParams p) {
   const int t = p.tile_begin + blockIdx.x;
   const int kvh = p.head_begin / p.group + blockIdx.y;
-  const int b = blockIdx.z;
+  const int b = blockIdx.z / kRescueSplits;
+  const int split = blockIdx.z % kRescueSplits;
   const int G = p.group;
   if (t == 0) return;  // tile 0 has no earlier block
   extern __shared__ __align__(16) uint8_t smem[];
   float *qm = reinterpret_cast<float *>(smem);                                 // [G][128]
-  float *red_v = qm + G * kHeadDim;                                            // [4][G]
-  int *red_i = reinterpret_cast<int *>(red_v + 4 * G);                         // [4][G]
+  float *part = qm + G * kHeadDim;                                             // [8][128]
+  float *red_v = part + 8 * kHeadDim;                                          // [8][G]
+  int *red_i = reinterpret_cast<int *>(red_v + 8 * G);                         // [8][G]
   const int words = (p.nb + 31) / 32;
-  uint32_t *bits = reinterpret_cast<uint32_t *>(red_i + 4 * G);                // [G][words]
+  uint32_t *bits = reinterpret_cast<uint32_t *>(red_i + 8 * G);                // [G][words]
+  uint16_t *ulist = reinterpret_cast<uint16_t *>(bits + G * words);            // [nb] union of the tails
+  int *scratch = reinterpret_cast<int *>(ulist + ((p.nb + 1) & ~1));           // [8]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   // Tail bits of the group's heads: the route's (fused path) or kb < t and not selected (op).
@@ -36,10 +44,10 @@ __global__ void __launch_bounds__(128) rescue_choice_kernel(MeanParams p) {
     const int h = kvh * G + g;
     if (kMode == kMeanMergeInPlace) {
       const uint32_t *src = p.route.tail + p.route.row(b, h, t, p.H) * p.route.words;
-      for (int w = tid; w < words; w += 128) bits[g * words + w] = src[w];
+      for (int w = tid; w < words; w += kChoiceThreads) bits[g * words + w] = src[w];
     } else {
       const int64_t col = ((int64_t)b * p.nb + t) * p.nb * p.H + h;
-      for (int k0 = 0; k0 < 32 * words; k0 += 128) {
+      for (int k0 = 0; k0 < 32 * words; k0 += kChoiceThreads) {
         const int kb = k0 + tid;
         const bool in = kb < t && p.mask[col + (int64_t)kb * p.H] == 0;
         const unsigned bal = __ballot_sync(0xffffffffu, in);
@@ -48,43 +56,72 @@ __global__ void __launch_bounds__(128) rescue_choice_kernel(MeanParams p) {
     }
   }
   __syncthreads();
-  {  // nothing to choose when no head of the group has a tail (every block selected)
-    int any = 0;
-    for (int i = tid; i < G * words; i += 128) any |= bits[i] != 0u;
-    if (!__syncthreads_or(any)) return;
+  // Union of the group's tails, ascending.
+  int nu = 0;
+  for (int w0 = 0; w0 < words; w0 += kChoiceThreads) {
+    const int w = w0 + tid;
+    uint32_t u = 0;
+    if (w < words)
+      for (int g = 0; g < G; ++g) u |= bits[g * words + w];
+    int total;
+    int pos = block_exclusive_scan<kChoiceThreads>(__popc(u), scratch, &total);
+    for (uint32_t x = u; x; x &= x - 1) ulist[nu + pos++] = (uint16_t)(32 * w + __ffs(x) - 1);
+    nu += total;
   }
-  // Query means (kernels.py:278-279): sum over the valid rows in fp32, then divide.
+  __syncthreads();
+  if (split >= nu) return;  // nothing for this CTA of the split (uniform)
+  // Query means (kernels.py:278-279): fp32 sums over the valid rows, then divided by the count.
+  // Warp w sums rows w, w + 8, ... for dimensions 4 lane .. 4 lane + 3; the eight partial sums
+  // are added in warp order.
   const int rows = min(kBlock, p.L - t * kBlock);
   for (int g = 0; g < G; ++g) {
     const int h = kvh * G + g;
-    const __nv_bfloat16 *src = p.q + b * p.q_sb + (int64_t)t * kBlock * p.q_sl + h * p.q_sh + tid;
-    float s = 0.f;
-#pragma unroll 8
-    for (int r = 0; r < rows; ++r) s += __bfloat162float(src[(int64_t)r * p.q_sl]);
-    qm[g * kHeadDim + tid] = s / (float)rows;
-  }
-  __syncthreads();
-
-  uint8_t *choice = p.choice;
-  for (int kb = 0; kb < t; ++kb) {
-    uint32_t any = 0;
-    for (int g = 0; g < G; ++g) any |= bits[g * words + (kb >> 5)];
-    if (!((any >> (kb & 31)) & 1u)) continue;  // uniform: no head has kb in its tail
-    // Token tid's key row, in registers.
-    uint32_t kr[64];
-    const uint4 *row = reinterpret_cast<const uint4 *>(p.k + b * p.k_sb + ((int64_t)kb * kBlock + tid) * p.k_sl +
-                                                       kvh * p.k_sh);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint4 u = row[i];
-      kr[4 * i] = u.x; kr[4 * i + 1] = u.y; kr[4 * i + 2] = u.z; kr[4 * i + 3] = u.w;
+    const __nv_bfloat16 *src = p.q + b * p.q_sb + (int64_t)t * kBlock * p.q_sl + h * p.q_sh + 4 * lane;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll 4
+    for (int r = warp; r < rows; r += 8) {
+      const uint2 u = *reinterpret_cast<const uint2 *>(src + (int64_t)r * p.q_sl);
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
+      const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
+      s0 += a.x; s1 += a.y; s2 += c.x; s3 += c.y;
     }
+    *reinterpret_cast<float4 *>(part + warp * kHeadDim + 4 * lane) = make_float4(s0, s1, s2, s3);
+    __syncthreads();
+    if (tid < kHeadDim) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) s += part[w * kHeadDim + tid];
+      qm[g * kHeadDim + tid] = s / (float)rows;
+    }
+    __syncthreads();
+  }
+
+  // Thread pair (2 j, 2 j + 1) holds token j's key row, 64 dimensions each.
+  const int tok = tid >> 1, half = tid & 1;
+  uint8_t *choice = p.choice;
+  auto load_row = [&](int kb, uint4 (&dst)[8]) {
+    const uint4 *row = reinterpret_cast<const uint4 *>(p.k + b * p.k_sb + ((int64_t)kb * kBlock + tok) * p.k_sl +
+                                                       kvh * p.k_sh + 64 * half);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[i] = row[i];
+  };
+  uint4 nxt[8];
+  load_row(ulist[split], nxt);
+  for (int e = split; e < nu; e += kRescueSplits) {
+    const int kb = ulist[e];
+    // The next block's half row is requested before this block's dots.
+    uint32_t kr[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      kr[4 * i] = nxt[i].x; kr[4 * i + 1] = nxt[i].y; kr[4 * i + 2] = nxt[i].z; kr[4 * i + 3] = nxt[i].w;
+    }
+    if (e + kRescueSplits < nu) load_row(ulist[e + kRescueSplits], nxt);
     for (int g = 0; g < G; ++g) {
       if (!((bits[g * words + (kb >> 5)] >> (kb & 31)) & 1u)) continue;  // uniform per head
-      const float4 *m4 = reinterpret_cast<const float4 *>(qm + g * kHeadDim);
+      const float4 *m4 = reinterpret_cast<const float4 *>(qm + g * kHeadDim + 64 * half);
       float dot = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         const float4 m = m4[i];
         const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[2 * i]));
         const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[2 * i + 1]));
@@ -93,11 +130,12 @@ __global__ void __launch_bounds__(128) rescue_choice_kernel(MeanParams p) {
         dot = fmaf(m.z, c.x, dot);
         dot = fmaf(m.w, c.y, dot);
       }
-      // (value, index) maximum, the lower index on ties.
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);  // the two halves, the same sum in both lanes
+      // (value, index) maximum over the warp's 16 tokens, the lower index on ties.
       float bv = dot;
-      int bi = tid;
+      int bi = tok;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
+      for (int o = 16; o > 1; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
         if (ov > bv || (ov == bv && oi < bi)) {
@@ -114,7 +152,7 @@ __global__ void __launch_bounds__(128) rescue_choice_kernel(MeanParams p) {
     if (tid < G && ((bits[tid * words + (kb >> 5)] >> (kb & 31)) & 1u)) {
       float bv = red_v[tid];
       int bi = red_i[tid];
-      for (int w = 1; w < 4; ++w) {
+      for (int w = 1; w < 8; ++w) {
         const float v = red_v[w * G + tid];
         const int i = red_i[w * G + tid];
         if (v > bv || (v == bv && i < bi)) {
@@ -132,17 +170,18 @@ __global__ void __launch_bounds__(128) rescue_choice_kernel(MeanParams p) {
 int launch_rescue_choice(const MeanParams &p, int mode, int tiles, int kv_count, int B, cudaStream_t s) {
   if (tiles <= 0 || kv_count <= 0) return FPX_OK;
   if (p.group > kRescueMaxGroup || !p.choice || !p.k) return FPX_ERR_UNSUPPORTED;
-  const size_t smem = (size_t)p.group * kHeadDim * 4 + 8 * p.group * 4 + (size_t)p.group * ((p.nb + 31) / 32) * 4;
+  const size_t smem = (size_t)p.group * kHeadDim * 4 + 8 * kHeadDim * 4 + 16 * p.group * 4 +
+                      (size_t)p.group * ((p.nb + 31) / 32) * 4 + (size_t)((p.nb + 1) & ~1) * 2 + 32;
   if (smem > 200 * 1024) return FPX_ERR_UNSUPPORTED;
-  const dim3 grid(tiles, kv_count, B);
+  const dim3 grid(tiles, kv_count, B * kRescueSplits);
   if (mode == kMeanMergeInPlace) {
     cudaFuncSetAttribute(rescue_choice_kernel<kMeanMergeInPlace>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-    rescue_choice_kernel<kMeanMergeInPlace><<<grid, 128, smem, s>>>(p);
+    rescue_choice_kernel<kMeanMergeInPlace><<<grid, kChoiceThreads, smem, s>>>(p);
   } else {
     cudaFuncSetAttribute(rescue_choice_kernel<kMeanStandalone>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-    rescue_choice_kernel<kMeanStandalone><<<grid, 128, smem, s>>>(p);
+    rescue_choice_kernel<kMeanStandalone><<<grid, kChoiceThreads, smem, s>>>(p);
   }
   FPX_CHECK_LAUNCH();
   return FPX_OK;

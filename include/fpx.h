@@ -67,12 +67,13 @@ int fpx_version(void);
 /* Process-wide options (no reference counterpart). Key 1 selects the exact-attention kernel of
  * fpx_prefill_attention and fpx_exact_attention at head dim 128: 0 = tcgen05/TMEM/TMA, two
  * query tiles per CTA (default), 1 = mma.sync (cross-check), 2 = tcgen05, one query tile per
- * CTA with double-buffered S (the kernel head dim 256 always uses). Key 2 sets how many of every 8 exp2 pairs the tcgen05 kernel evaluates with
- * an FMA-pipe polynomial instead of the special-function unit: 0 (default), 2 or 3. Key 3
- * selects the V1 routing kernel (fpx_prefill_attention and fpx_v1_scores): 0 = tcgen05,
- * transposed block-mean x Q products in TMEM (default), 1 = mma.sync (cross-check). Key 4
- * selects the mean-tail kernel of fpx_prefill_attention: 0 = tcgen05, block means as bf16
- * high + low halves (default), 1 = fp32 CUDA cores (cross-check). Key 5 selects the
+ * CTA with double-buffered S (the kernel head dim 256 always uses). Key 2 sets how many of
+ * every 8 exp2 pairs the tcgen05 kernel evaluates with an FMA-pipe polynomial instead of the
+ * special-function unit: 0 (default), 2 or 3. Key 3 selects the V1 routing kernel
+ * (fpx_prefill_attention and fpx_v1_scores): 0 = tcgen05, transposed block-mean x Q products
+ * in TMEM (default), 1 = mma.sync (cross-check). Key 4 selects the tail kernels of
+ * fpx_prefill_attention: 0 = tcgen05 (default; block means as bf16 high + low halves, rescue
+ * rows gathered into swizzled tiles), 1 = fp32 CUDA cores (cross-check). Key 5 selects the
  * routing kernel of the new selectors in fpx_prefill_attention: 0 = tcgen05, descriptors as
  * bf16 high + low halves, two passes (default), 1 = fp32 CUDA cores (cross-check). */
 int fpx_set_option(int key, int value);

@@ -402,6 +402,30 @@ def test_tcgen05_and_fp32_mean_tails_agree(length, heads, kv):
     assert _capi.device_error() == 0
 
 
+@pytest.mark.parametrize("method", ["fp_v1_rescue", "fp_v1_rescue_v2"])
+@pytest.mark.parametrize("length,heads,kv", [(4096, 28, 4), (40000, 10, 2)])
+def test_tcgen05_and_fp32_rescue_tails_agree(method, length, heads, kv):
+    """The tensor-core rescue tail (gathered rescue rows; for _v2 the remainder means as bf16
+    high + low halves) against the fp32 CUDA-core tail on structured inputs with real tails;
+    40000 tokens give 313 blocks, so late tiles have three chunks of tail keys per pass."""
+    shape = synthetic.LayerShape(1, length, heads, kv)
+    q, k, v = cuda(*synthetic.attention_inputs(shape, seed=length + 2, needles=3, structured_sigma=0.5))
+    results = []
+    try:
+        for which in ("fp32", "tcgen05"):
+            _capi.set_mean_kernel(which)
+            lse = torch.empty(1, length, heads, device=DEV)
+            out = ops.prefill_attention(q, k, v, method, 0.08, SCALE, lse=lse)
+            results.append((out, lse))
+    finally:
+        _capi.set_mean_kernel("tcgen05")
+    sel = ops.export_routing(method, 1, length, heads, kv)[0]
+    assert int(sel.sum()) < heads * oracle.num_blocks(length) * (oracle.num_blocks(length) + 1) // 2  # tails exist
+    torch.testing.assert_close(results[1][0].float(), results[0][0].float(), atol=O_TOL, rtol=0)
+    torch.testing.assert_close(results[1][1], results[0][1], atol=LSE_TOL, rtol=0)
+    assert _capi.device_error() == 0
+
+
 @pytest.mark.parametrize("method", ["mean_balanced", "cgf_mean", "dispersion_mean"])
 @pytest.mark.parametrize("length,heads,kv", [(4096, 14, 2), (40000, 10, 2)])
 def test_tcgen05_and_fp32_selector_routing_agree(method, length, heads, kv):
