@@ -3,9 +3,10 @@
 A decode step all-reduces a 7 KB hidden vector twice per layer; a collective library spends
 tens of microseconds per such call. ``PeerAllReduce`` maps one small buffer per rank into every
 peer's address space (CUDA IPC, handles exchanged through the process group once) and runs
-``fpx_allreduce_bf16``: each rank publishes its input, waits for its peers' flags (bounded
-waits) and sums the ranks' copies in rank order, so every rank gets the same bits. The call's
-counter lives in device memory, so the kernel can be captured in a CUDA graph and replayed.
+``fpx_allreduce_bf16``: each rank stores its input and a flag into every rank's buffer, waits
+for the flags in its own buffer (bounded waits) and sums the ranks' copies there in rank
+order, so every rank gets the same bits. The call's counter lives in device memory, so the
+kernel can be captured in a CUDA graph and replayed.
 """
 
 from __future__ import annotations

@@ -3,17 +3,18 @@
 // decode step, where a collective library's per-call latency dominates 7 KB messages.
 //
 // Every rank owns one buffer, mapped into every peer's address space through CUDA IPC:
-//   [0]   flag  (u32): the last call whose input this rank has published
-//   [64]  epoch (u32): this rank's call counter (device memory, so CUDA-graph replays advance it)
-//   [128] error (i32): set when a wait gave up
-//   [256] slot 0, then slot 1: max_elems bf16 each
-// Call e = epoch + 1:
-//   1. wait until every peer's flag >= e - 1. Each peer has then entered call e - 1, so it has
-//      finished reading slot e & 1 of call e - 2 (a rank's kernels run in order);
-//   2. copy the input into this rank's slot e & 1, fence at system scope, publish flag = e;
-//   3. wait until every peer's flag >= e;
-//   4. sum the ranks' slots in rank order in fp32 (the same order everywhere, so every rank gets
-//      the same bits) and write the bf16 result over the input.
+//   [0]    error (i32): set when a wait gave up
+//   [64]   epoch (u32): this rank's call counter (device memory, so CUDA-graph replays advance it)
+//   [256 + 64 q]  flag of rank q (u32): the last call whose input rank q has pushed here
+//   [768]  slots [2][kArMaxRanks][max_elems] bf16: rank q's input of calls with parity e & 1
+// Call e = epoch + 1 on rank r (a push: every remote access is a store):
+//   1. store the input into slot [e & 1][r] of every rank's buffer (its own included), fence at
+//      system scope, then store flag e into flag r of every rank's buffer (release);
+//   2. wait until every flag in this rank's own buffer is >= e (acquire, local polling);
+//   3. sum the ranks' slots [e & 1][q] in rank order in fp32 (the same order everywhere, so
+//      every rank gets the same bits) and write the bf16 result over the input.
+// Slot [e & 1][r] of rank p is free when r writes it: r finished call e - 1, so it saw p's
+// flag e - 1, which p stored after finishing call e - 2, the last reader of that slot.
 // Every wait is bounded (about 1 s of clock64); a wait that gives up sets the error word and the
 // kernel returns, so a missing rank ends the call instead of hanging the GPU.
 #include <cstring>
@@ -25,6 +26,7 @@ namespace fpx {
 constexpr int kArMaxRanks = 8;
 constexpr int kArThreads = 512;
 constexpr long long kArWaitCycles = 1ll << 31;
+constexpr size_t kArFlags = 256, kArSlots = 768;
 
 struct ArPeers {
   uint8_t *base[kArMaxRanks];
@@ -60,8 +62,8 @@ __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(__nv_bflo
   __shared__ uint32_t s_epoch;
   __shared__ int s_fail;
   uint8_t *own = peers.base[rank];
+  int *error = reinterpret_cast<int *>(own);
   uint32_t *epoch = reinterpret_cast<uint32_t *>(own + 64);
-  int *error = reinterpret_cast<int *>(own + 128);
   if (threadIdx.x == 0) {
     s_epoch = *epoch + 1;
     s_fail = *reinterpret_cast<volatile int *>(error);
@@ -69,38 +71,34 @@ __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(__nv_bflo
   __syncthreads();
   if (s_fail) return;  // an earlier call already failed: the buffers are out of step
   const uint32_t e = s_epoch;
-  auto flag = [&](int r) { return reinterpret_cast<uint32_t *>(peers.base[r]); };
-  auto slot = [&](int r) {
-    return reinterpret_cast<uint4 *>(peers.base[r] + 256 + (size_t)(e & 1u) * max_elems * 2);
+  auto flag = [&](int buf, int q) { return reinterpret_cast<uint32_t *>(peers.base[buf] + kArFlags + 64 * q); };
+  auto slot = [&](int buf, int q) {
+    return reinterpret_cast<uint4 *>(peers.base[buf] + kArSlots +
+                                     ((size_t)(e & 1u) * kArMaxRanks + q) * (size_t)max_elems * 2);
   };
-  // 1. every peer is past call e - 2
-  if (threadIdx.x < world && threadIdx.x != rank && !ar_wait(flag(threadIdx.x), e - 1)) atomicExch(&s_fail, 1);
-  __syncthreads();
-  if (s_fail) {
-    if (threadIdx.x == 0) atomicExch(error, 1);
-    return;
-  }
-  // 2. publish this rank's input
+  // 1. push this rank's input into every rank's slot, then the flags
   const int n8 = n / 8;  // 16-byte pieces (n % 8 == 0 is checked on the host)
-  uint4 *mine = slot(rank);
   const uint4 *src = reinterpret_cast<const uint4 *>(inout);
-  for (int i = threadIdx.x; i < n8; i += kArThreads) mine[i] = src[i];
+  for (int i = threadIdx.x; i < n8; i += kArThreads) {
+    const uint4 v = src[i];
+    for (int p = 0; p < world; ++p) slot(p, rank)[i] = v;
+  }
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) st_release_sys(flag(rank), e);
-  // 3. every peer has published call e
-  if (threadIdx.x < world && threadIdx.x != rank && !ar_wait(flag(threadIdx.x), e)) atomicExch(&s_fail, 1);
+  if (threadIdx.x < world) st_release_sys(flag(threadIdx.x, rank), e);
+  // 2. every rank's input of call e has arrived here
+  if (threadIdx.x < world && !ar_wait(flag(rank, threadIdx.x), e)) atomicExch(&s_fail, 1);
   __syncthreads();
   if (s_fail) {
     if (threadIdx.x == 0) atomicExch(error, 1);
     return;
   }
-  // 4. sum in rank order
+  // 3. sum in rank order (local slots; relaxed system-scope loads bypass stale L1 lines)
   uint4 *dst = reinterpret_cast<uint4 *>(inout);
   for (int i = threadIdx.x; i < n8; i += kArThreads) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int r = 0; r < world; ++r) {
-      const uint4 v = ld_relaxed_sys_v4(slot(r) + i);
+    for (int q = 0; q < world; ++q) {
+      const uint4 v = ld_relaxed_sys_v4(slot(rank, q) + i);
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -121,11 +119,11 @@ using namespace fpx;
 
 extern "C" size_t fpx_ar_buffer_bytes(int max_elems) {
   if (max_elems <= 0 || max_elems % 8) return 0;
-  return 256 + (size_t)2 * max_elems * 2;
+  return kArSlots + (size_t)2 * kArMaxRanks * max_elems * 2;
 }
 
 extern "C" int fpx_ar_create(size_t bytes, void **base, void *ipc_handle) {
-  if (!base || !ipc_handle || bytes < 256) return FPX_ERR_INVALID;
+  if (!base || !ipc_handle || bytes < kArSlots) return FPX_ERR_INVALID;
   void *p = nullptr;
   if (cudaMalloc(&p, bytes) != cudaSuccess) return FPX_ERR_CUDA;
   if (cudaMemset(p, 0, bytes) != cudaSuccess ||
@@ -169,7 +167,7 @@ extern "C" int fpx_allreduce_bf16(void *inout, int64_t n, void *const *bases, in
 
 extern "C" int fpx_ar_error(const void *base, int *code) {
   if (!base || !code) return FPX_ERR_INVALID;
-  return cudaMemcpy(code, static_cast<const uint8_t *>(base) + 128, sizeof(int), cudaMemcpyDeviceToHost) ==
+  return cudaMemcpy(code, static_cast<const uint8_t *>(base), sizeof(int), cudaMemcpyDeviceToHost) ==
                  cudaSuccess
              ? FPX_OK
              : FPX_ERR_CUDA;

@@ -177,8 +177,10 @@ int fpx_merge_exact_mean(const void *exact_out, const float *exact_lse, const fl
  * fpx_ar_buffer_bytes(max_elems) (fpx_ar_create: cudaMalloc'd and zeroed, with its CUDA IPC
  * handle, 64 bytes), the ranks exchange handles and map their peers' buffers (fpx_ar_open), and
  * every rank then calls fpx_allreduce_bf16 with the world's buffer bases in rank order (its own
- * at index rank). The sum is taken in rank order in fp32, so all ranks get the same bits; the
- * call counter lives in the buffer, so calls can be captured in a CUDA graph. Waits for peers
+ * at index rank; at most 8 ranks). A call stores the rank's input and a flag into every rank's
+ * buffer, polls the flags of its own buffer and sums its own slots. The sum is taken in rank
+ * order in fp32, so all ranks get the same bits; the call counter lives in the buffer, so calls
+ * can be captured in a CUDA graph. Waits for peers
  * are bounded; a wait that gives up sets the buffer's error word (fpx_ar_error) and later calls
  * return at once. Set-up allocates; the calls do not. */
 size_t fpx_ar_buffer_bytes(int max_elems);
