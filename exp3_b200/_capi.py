@@ -142,7 +142,7 @@ def device_error(reset: bool = True) -> int:
 
 
 def set_exact_kernel(name: str) -> None:
-    """Selects the exact-attention kernel of the fused path: "tcgen05" (two query tiles per CTA),
+    """Selects the exact-attention kernel at head dim 128: "tcgen05" (two query tiles per CTA),
     "tcgen05_single" (one tile per CTA, double-buffered S) or "mma" (the mma.sync cross-check)."""
     call("fpx_set_option", 1, {"tcgen05": 0, "mma": 1, "tcgen05_single": 2}[name])
 

@@ -1,4 +1,4 @@
-// The softmax step shared by the tcgen05 exact kernels (attn_tc.cu, attn_tc1.cu, attn_tc2.cu):
+// The softmax step shared by the tcgen05 exact kernels (attn_tc.cu, attn_tc1.cu):
 // one thread owns one query row (one TMEM lane) of a block of NC keys (128, or a 64-key half).
 #pragma once
 

@@ -317,21 +317,23 @@ def test_tcgen05_and_mma_exact_kernels_agree():
     assert _capi.device_error() == 0
 
 
+@pytest.mark.parametrize("kernel", ["tcgen05_single"])
 @pytest.mark.parametrize("method", ["mean_native", "fp_v1", "dense", "cgf_mean"])
-def test_single_tile_exact_kernel_matches_oracle(method):
+def test_single_tile_exact_kernel_matches_oracle(method, kernel):
     """The one-tile-per-CTA tcgen05 kernel (double-buffered S) at head dim 128, selected with
-    fpx_set_option(1, 2): the fused path against the oracle, ragged last tile, B = 2."""
+    fpx_set_option(1, 2): the fused path against the oracle, ragged last tile, B = 2, heads of an
+    odd group (7) included."""
     shape = synthetic.LayerShape(2, 2177, 14, 2)
     q, k, v = synthetic.attention_inputs(shape, seed=12, needles=4, structured_sigma=0.5)
     try:
-        _capi.set_exact_kernel("tcgen05_single")
+        _capi.set_exact_kernel(kernel)
         run_fused_vs_oracle(method, q, k, v, 0.08, list(range(oracle.num_blocks(2177))))
     finally:
         _capi.set_exact_kernel("tcgen05")
     assert _capi.device_error() == 0
 
 
-def test_single_tile_exact_kernel_reference_layout_and_agreement():
+def test_alternative_exact_kernels_reference_layout_and_agreement():
     data, q, k, v = load("exact_mean_l257.npz")
     qd, kd, vd = cuda(q, k, v)
     idx, cnt = t(data["indices_fixed"]).to(DEV), t(data["counts_fixed"]).to(DEV)
@@ -348,7 +350,7 @@ def test_single_tile_exact_kernel_reference_layout_and_agreement():
             results.append((ops.prefill_attention(q2, k2, v2, "mean_native", 0.08, SCALE, lse=lse2), lse2))
     finally:
         _capi.set_exact_kernel("tcgen05")
-    # 32K: the two tcgen05 kernels agree (same products, same rounding points)
+    # 32K: the tcgen05 kernels agree (same products, same rounding points)
     torch.testing.assert_close(results[0][0].float(), results[1][0].float(), atol=O_TOL, rtol=0)
     torch.testing.assert_close(results[0][1], results[1][1], atol=LSE_TOL, rtol=0)
     assert _capi.device_error() == 0
