@@ -477,12 +477,18 @@ def main():
     # step i computes, and step i's D2H on a second copy stream while step i+1 computes.
     h0, h1 = kv_range[0] * group, kv_range[1] * group
     t0, t1 = tile_range
-    q_h = q[:, :, h0:h1].contiguous().cpu().pin_memory()
-    k_h = k[:, :, kv_range[0]:kv_range[1]].contiguous().cpu().pin_memory()
-    v_h = v[:, :, kv_range[0]:kv_range[1]].contiguous().cpu().pin_memory()
+    # The pipeline streams work units: one per KV group this rank owns when it owns whole groups
+    # (each group is an independent attention problem: its query heads, its K and V), else the
+    # rank's tile shard. Per unit, the H2D of the next unit overlaps this unit's compute and the
+    # D2H of the previous one, so only one unit's copies are left outside the overlap.
+    full_tiles = tile_range == (0, blocks)
+    units = [(g, g + 1) for g in range(kv_range[0], kv_range[1])] if full_tiles else [tuple(kv_range)]
+    host = [tuple(x.contiguous().cpu().pin_memory() for x in (q[:, :, a * group:c * group], k[:, :, a:c], v[:, :, a:c]))
+            for a, c in units]
     slots = 2
-    o_hs = [torch.empty(b, (t1 - t0) * 128, h1 - h0, d, dtype=torch.bfloat16).pin_memory() for _ in range(slots)]
-    dev_in = [[torch.empty_like(x, device=dev) for x in (q_h, k_h, v_h)] for _ in range(slots)]
+    o_hs = [[torch.empty(b, (t1 - t0) * 128, (c - a) * group, d, dtype=torch.bfloat16).pin_memory() for a, c in units]
+            for _ in range(slots)]
+    dev_in = [[[torch.empty_like(x, device=dev) for x in unit] for unit in host] for _ in range(slots)]
     backend = AttentionBackend(alpha=alpha)
     backend.configure(method)
     compute = torch.cuda.current_stream(dev)
@@ -492,33 +498,34 @@ def main():
         layer_idx = 0
 
     def e2e_run(n, start=None, end=None):
-        in_free = [None] * slots  # compute has finished reading the slot
+        in_free = [[None] * len(units) for _ in range(slots)]  # compute has finished reading the slot
         with torch.cuda.stream(h2d_stream):
             if start is not None:
                 start.record(h2d_stream)
         for i in range(n):
             sl = i % slots
-            qd, kd, vd = dev_in[sl]
-            with torch.cuda.stream(h2d_stream):
-                if in_free[sl] is not None:
-                    h2d_stream.wait_event(in_free[sl])
-                for dst, src in zip(dev_in[sl], (q_h, k_h, v_h)):
-                    dst.copy_(src, non_blocking=True)
-                ready = torch.cuda.Event()
-                ready.record(h2d_stream)
-            compute.wait_event(ready)
-            if tile_range == (0, blocks):
-                o, _ = backend.forward(Layer(), qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2), None,
-                                       scale)
-            else:  # a tile shard: the same fused op with this rank's tile range
-                o = ops.prefill_attention(qd, kd, vd, method, alpha, scale, tile_range=tile_range)
-            done = torch.cuda.Event()
-            done.record(compute)
-            in_free[sl] = done
-            with torch.cuda.stream(d2h_stream):
-                d2h_stream.wait_event(done)
-                o_hs[sl].copy_(o[:, t0 * 128:t1 * 128], non_blocking=True)
-            o.record_stream(d2h_stream)
+            for u in range(len(units)):
+                qd, kd, vd = dev_in[sl][u]
+                with torch.cuda.stream(h2d_stream):
+                    if in_free[sl][u] is not None:
+                        h2d_stream.wait_event(in_free[sl][u])
+                    for dst, src in zip(dev_in[sl][u], host[u]):
+                        dst.copy_(src, non_blocking=True)
+                    ready = torch.cuda.Event()
+                    ready.record(h2d_stream)
+                compute.wait_event(ready)
+                if full_tiles:
+                    o, _ = backend.forward(Layer(), qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2), None,
+                                           scale)
+                else:  # a tile shard: the same fused op with this rank's tile range
+                    o = ops.prefill_attention(qd, kd, vd, method, alpha, scale, tile_range=tile_range)
+                done = torch.cuda.Event()
+                done.record(compute)
+                in_free[sl][u] = done
+                with torch.cuda.stream(d2h_stream):
+                    d2h_stream.wait_event(done)
+                    o_hs[sl][u].copy_(o[:, t0 * 128:t1 * 128], non_blocking=True)
+                o.record_stream(d2h_stream)
         if end is not None:
             end.record(d2h_stream)
 
@@ -534,9 +541,8 @@ def main():
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t)
-    o_h = o_hs[0]
-    h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h))
-    d2h = o_h.numel() * o_h.element_size()
+    h2d = sum(x.numel() * x.element_size() for unit in host for x in unit)
+    d2h = sum(o.numel() * o.element_size() for o in o_hs[0])
     if world > 1:
         counts = torch.tensor([float(h2d), float(d2h)], device=dev)
         dist.all_reduce(counts)
@@ -578,7 +584,8 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "pipeline": "2 input slots; H2D / compute / D2H of successive steps overlap on 3 streams"},
+                    "pipeline": f"{len(units)} unit(s) per step (KV groups, or the rank's tile shard), 2 input "
+                                "slots per unit; H2D / compute / D2H of successive units overlap on 3 streams"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
         }
