@@ -27,25 +27,27 @@ struct DecodeParams {
   int Lq, S, H, Hkv, group, splits, keys_per_split;
   const int32_t *S_dev;  // if set, the number of keys is read here (S is then the capacity)
   float scale_log2;
-  float *part_o;  // [B*Lq][H][splits][128]
+  float *part_o;  // [B*Lq][H][splits][d]
   float *part_ml; // [B*Lq][H][splits][2]
 };
 
 constexpr int kDecodeChunk = 64;   // keys per pipeline stage: 16 per warp
 constexpr int kMaxSplits = 1024;
 
-// XOR-swizzled [rows][128] bf16 tile: 16-byte chunk c of row r lives at chunk c ^ (r & 7).
-FPX_INLINE int dswz(int r, int chunk) { return r * kHeadDim + ((chunk ^ (r & 7)) << 3); }
+// XOR-swizzled [rows][D] bf16 tile: 16-byte chunk c of row r lives at chunk c ^ (r & 7).
+template <int D>
+FPX_INLINE int dswz(int r, int chunk) { return r * D + ((chunk ^ (r & 7)) << 3); }
 
+template <int D>
 struct DecodeSmem {
-  __nv_bfloat16 q[16 * kHeadDim];  // the group's query rows (rows >= G zero), swizzled
+  __nv_bfloat16 q[16 * D];  // the group's query rows (rows >= G zero), swizzled
   union {
     struct {
-      __nv_bfloat16 k[2][kDecodeChunk * kHeadDim];  // swizzled K / V stages
-      __nv_bfloat16 v[2][kDecodeChunk * kHeadDim];
+      __nv_bfloat16 k[2][kDecodeChunk * D];  // swizzled K / V stages
+      __nv_bfloat16 v[2][kDecodeChunk * D];
     } stage;
     struct {
-      float o[4][16][kHeadDim];  // each warp's O for the 16 rows
+      float o[4][16][D];  // each warp's O for the 16 rows
       float m[4][16], l[4][16];
     } merge;
   } u;
@@ -55,20 +57,22 @@ struct DecodeSmem {
 // the KV group are the M = 16 rows (padded), keys stream 64 per stage through shared memory and
 // warp w takes keys 16w..16w+15 of every stage with its own online softmax (exp2 units); P is
 // rounded to bf16 for P.V. At the end the four warps' (m, l, O) are merged into the split's
-// partial.
+// partial. D is the head dim (128 or 256).
+template <int D>
 __global__ void __launch_bounds__(128) decode_split_kernel(DecodeParams p) {
+  constexpr int kChunks = D / 8;  // 16-byte pieces per row
   const int split = blockIdx.x, kvh = blockIdx.y, bq = blockIdx.z;
   const int b = bq / p.Lq, row = bq % p.Lq;
   const int G = p.group, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, tq = lane & 3;
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  DecodeSmem &sh = *reinterpret_cast<DecodeSmem *>(smem_raw);
-  for (int i = tid; i < 16 * 16; i += 128) {  // 16 rows x 16 chunks of 8 bf16
-    const int r = i >> 4, ch = i & 15;
+  DecodeSmem<D> &sh = *reinterpret_cast<DecodeSmem<D> *>(smem_raw);
+  for (int i = tid; i < 16 * kChunks; i += 128) {  // 16 rows x D/8 chunks of 8 bf16
+    const int r = i / kChunks, ch = i % kChunks;
     uint4 val = make_uint4(0, 0, 0, 0);
     if (r < G)
       val = *reinterpret_cast<const uint4 *>(p.q + b * p.q_sb + (int64_t)row * p.q_sl + (kvh * G + r) * p.q_sh + 8 * ch);
-    *reinterpret_cast<uint4 *>(&sh.q[dswz(r, ch)]) = val;
+    *reinterpret_cast<uint4 *>(&sh.q[dswz<D>(r, ch)]) = val;
   }
   const int S = p.S_dev ? min(*p.S_dev, p.S) : p.S;
   const int k0 = split * p.keys_per_split;
@@ -78,28 +82,28 @@ __global__ void __launch_bounds__(128) decode_split_kernel(DecodeParams p) {
   const __nv_bfloat16 *vbase = p.v + b * p.v_sb + kvh * p.v_sh;
   auto stage = [&](int c) {
     const int st = c & 1, base = k0 + c * kDecodeChunk;
-    for (int i = tid; i < kDecodeChunk * 16; i += 128) {
-      const int r = i >> 4, ch = i & 15;
+    for (int i = tid; i < kDecodeChunk * kChunks; i += 128) {
+      const int r = i / kChunks, ch = i % kChunks;
       const bool ok = base + r < k1;
       const int64_t key = ok ? base + r : k0;
-      cp_async16(&sh.u.stage.k[st][dswz(r, ch)], kbase + key * p.k_sl + 8 * ch, ok);
-      cp_async16(&sh.u.stage.v[st][dswz(r, ch)], vbase + key * p.v_sl + 8 * ch, ok);
+      cp_async16(&sh.u.stage.k[st][dswz<D>(r, ch)], kbase + key * p.k_sl + 8 * ch, ok);
+      cp_async16(&sh.u.stage.v[st][dswz<D>(r, ch)], vbase + key * p.v_sl + 8 * ch, ok);
     }
     cp_async_commit();
   };
   if (chunks > 0) stage(0);
   __syncthreads();
-  uint32_t qf[8][4];
+  uint32_t qf[D / 16][4];
   {
     const int m = lane >> 3;
     const int r = ((m & 1) << 3) + (lane & 7);
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-      ldmatrix_x4(qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], smem_u32(&sh.q[dswz(r, 2 * kk + (m >> 1))]));
+    for (int kk = 0; kk < D / 16; ++kk)
+      ldmatrix_x4(qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], smem_u32(&sh.q[dswz<D>(r, 2 * kk + (m >> 1))]));
   }
-  float o[16][4];
+  float o[D / 8][4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
   for (int c = 0; c < chunks; ++c) {
     const int st = c & 1;
@@ -116,11 +120,11 @@ __global__ void __launch_bounds__(128) decode_split_kernel(DecodeParams p) {
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
 #pragma unroll
-    for (int kk2 = 0; kk2 < 4; ++kk2) {
+    for (int kk2 = 0; kk2 < D / 32; ++kk2) {
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(b0, b1, b2, b3, smem_u32(ck + dswz(16 * warp + 8 * nt + (lane & 7), 4 * kk2 + (lane >> 3))));
+        ldmatrix_x4(b0, b1, b2, b3, smem_u32(ck + dswz<D>(16 * warp + 8 * nt + (lane & 7), 4 * kk2 + (lane >> 3))));
         mma_bf16_16816(sacc[nt], qf[2 * kk2], b0, b1);
         mma_bf16_16816(sacc[nt], qf[2 * kk2 + 1], b2, b3);
       }
@@ -160,15 +164,15 @@ __global__ void __launch_bounds__(128) decode_split_kernel(DecodeParams p) {
     lrow[0] = lrow[0] * corr[0] + rs[0];
     lrow[1] = lrow[1] * corr[1] + rs[1];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < D / 8; ++i) {
       o[i][0] *= corr[0]; o[i][1] *= corr[0];
       o[i][2] *= corr[1]; o[i][3] *= corr[1];
     }
     const int vr = 16 * warp + (lane & 7) + (((lane >> 3) & 1) << 3);
 #pragma unroll
-    for (int dn2 = 0; dn2 < 8; ++dn2) {
+    for (int dn2 = 0; dn2 < D / 16; ++dn2) {
       uint32_t b0, b1, b2, b3;
-      ldmatrix_x4_trans(b0, b1, b2, b3, smem_u32(cv + dswz(vr, 2 * dn2 + (lane >> 4))));
+      ldmatrix_x4_trans(b0, b1, b2, b3, smem_u32(cv + dswz<D>(vr, 2 * dn2 + (lane >> 4))));
       mma_bf16_16816(o[2 * dn2], pa, b0, b1);
       mma_bf16_16816(o[2 * dn2 + 1], pa, b2, b3);
     }
@@ -187,7 +191,7 @@ __global__ void __launch_bounds__(128) decode_split_kernel(DecodeParams p) {
     sh.u.merge.l[warp][g8 + 8] = lrow[1];
   }
 #pragma unroll
-  for (int dt = 0; dt < 16; ++dt) {
+  for (int dt = 0; dt < D / 8; ++dt) {
     const int col = 8 * dt + 2 * tq;
     sh.u.merge.o[warp][g8][col] = o[dt][0];
     sh.u.merge.o[warp][g8][col + 1] = o[dt][1];
@@ -199,18 +203,20 @@ __global__ void __launch_bounds__(128) decode_split_kernel(DecodeParams p) {
     float mm = -INFINITY;
 #pragma unroll
     for (int w = 0; w < 4; ++w) mm = fmaxf(mm, sh.u.merge.m[w][r]);
-    float ll = 0.f, oo = 0.f;
+    float ll = 0.f, oo[D / 128] = {};
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const float mw = sh.u.merge.m[w][r];
       if (mw == -INFINITY) continue;
       const float sc = exp2f(mw - mm);
       ll += sh.u.merge.l[w][r] * sc;
-      oo += sh.u.merge.o[w][r][tid] * sc;
+#pragma unroll
+      for (int c = 0; c < D / 128; ++c) oo[c] += sh.u.merge.o[w][r][tid + 128 * c] * sc;
     }
     const int h = kvh * G + r;
     const int64_t slot = ((int64_t)bq * p.H + h) * p.splits + split;
-    p.part_o[slot * kHeadDim + tid] = oo;
+#pragma unroll
+    for (int c = 0; c < D / 128; ++c) p.part_o[slot * D + tid + 128 * c] = oo[c];
     if (tid == 0) {
       p.part_ml[2 * slot] = mm;
       p.part_ml[2 * slot + 1] = ll;
@@ -218,30 +224,31 @@ __global__ void __launch_bounds__(128) decode_split_kernel(DecodeParams p) {
   }
 }
 
-__global__ void __launch_bounds__(128) decode_combine_kernel(DecodeParams p) {
+template <int D>
+__global__ void __launch_bounds__(D) decode_combine_kernel(DecodeParams p) {
   const int h = blockIdx.x, bq = blockIdx.y;
   const int b = bq / p.Lq, row = bq % p.Lq;
   const int64_t base = ((int64_t)bq * p.H + h) * p.splits;
   __shared__ float w[kMaxSplits];
-  __shared__ float red[4];
+  __shared__ float red[D / 32];
   float m = -INFINITY;
-  for (int s = threadIdx.x; s < p.splits; s += 128) m = fmaxf(m, p.part_ml[2 * (base + s)]);
-  m = block_max<128>(m, red);
+  for (int s = threadIdx.x; s < p.splits; s += D) m = fmaxf(m, p.part_ml[2 * (base + s)]);
+  m = block_max<D>(m, red);
   float l = 0.f;
-  for (int s = threadIdx.x; s < p.splits; s += 128) {
+  for (int s = threadIdx.x; s < p.splits; s += D) {
     const float ms = p.part_ml[2 * (base + s)];
     const float ws = ms == -INFINITY ? 0.f : exp2f(ms - m);
     w[s] = ws;
     l += p.part_ml[2 * (base + s) + 1] * ws;
   }
-  l = block_sum<128>(l, red);  // its barriers also publish w[]
+  l = block_sum<D>(l, red);  // its barriers also publish w[]
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // eight loads in flight
   int s = 0;
   for (; s + 8 <= p.splits; s += 8) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] += p.part_o[(base + s + e) * kHeadDim + threadIdx.x] * w[s + e];
+    for (int e = 0; e < 8; ++e) acc[e] += p.part_o[(base + s + e) * D + threadIdx.x] * w[s + e];
   }
-  for (; s < p.splits; ++s) acc[0] += p.part_o[(base + s) * kHeadDim + threadIdx.x] * w[s];
+  for (; s < p.splits; ++s) acc[0] += p.part_o[(base + s) * D + threadIdx.x] * w[s];
   const float o = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
   const float inv = l > 0.f ? 1.f / l : 0.f;
   p.out[b * p.o_sb + (int64_t)row * p.o_sl + h * p.o_sh + threadIdx.x] = __float2bfloat16_rn(o * inv);
@@ -250,15 +257,20 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeParams p) {
 }
 
 // Both decode kernels with the pipeline's shared memory.
-static int decode_launch(const DecodeParams &p, int B, int Hkv, cudaStream_t stream) {
-  if (p.splits > kMaxSplits) return FPX_ERR_UNSUPPORTED;
-  const int smem = (int)sizeof(DecodeSmem);
-  cudaFuncSetAttribute(decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  decode_split_kernel<<<dim3(p.splits, Hkv, B * p.Lq), 128, smem, stream>>>(p);
+template <int D>
+static int decode_launch_d(const DecodeParams &p, int B, int Hkv, cudaStream_t stream) {
+  const int smem = (int)sizeof(DecodeSmem<D>);
+  cudaFuncSetAttribute(decode_split_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  decode_split_kernel<D><<<dim3(p.splits, Hkv, B * p.Lq), 128, smem, stream>>>(p);
   FPX_CHECK_LAUNCH();
-  decode_combine_kernel<<<dim3(p.H, B * p.Lq), 128, 0, stream>>>(p);
+  decode_combine_kernel<D><<<dim3(p.H, B * p.Lq), D, 0, stream>>>(p);
   FPX_CHECK_LAUNCH();
   return FPX_OK;
+}
+
+static int decode_launch(const DecodeParams &p, int d, int B, int Hkv, cudaStream_t stream) {
+  if (p.splits > kMaxSplits) return FPX_ERR_UNSUPPORTED;
+  return d == 256 ? decode_launch_d<256>(p, B, Hkv, stream) : decode_launch_d<kHeadDim>(p, B, Hkv, stream);
 }
 
 static int decode_splits(int B, int Lq, int Hkv, int S) {
@@ -273,9 +285,9 @@ static int decode_splits(int B, int Lq, int Hkv, int S) {
 using namespace fpx;
 
 extern "C" size_t fpx_decode_workspace_bytes(int B, int Lq, int H, int Hkv, int S, int d) {
-  if (B <= 0 || Lq <= 0 || H <= 0 || Hkv <= 0 || S <= 0 || d != kHeadDim) return 0;
+  if (B <= 0 || Lq <= 0 || H <= 0 || Hkv <= 0 || S <= 0 || (d != kHeadDim && d != 256)) return 0;
   const size_t splits = decode_splits(B, Lq, Hkv, S);
-  return (size_t)B * Lq * H * splits * (kHeadDim + 2) * sizeof(float);
+  return (size_t)B * Lq * H * splits * (d + 2) * sizeof(float);
 }
 
 static int decode_run(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh, const void *k, int64_t k_sb,
@@ -283,7 +295,7 @@ static int decode_run(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh, c
                       int Lq, int S, const int32_t *S_dev, int H, int Hkv, int d, double scale, void *out,
                       int64_t o_sb, int64_t o_sl, int64_t o_sh, float *lse, void *workspace,
                       size_t workspace_bytes, cudaStream_t stream) {
-  if (d != kHeadDim) return FPX_ERR_UNSUPPORTED;
+  if (d != kHeadDim && d != 256) return FPX_ERR_UNSUPPORTED;
   if (!q || !k || !v || !out || B <= 0 || Lq <= 0 || S <= 0 || H <= 0 || Hkv <= 0)
     return FPX_ERR_INVALID;
   // Q, K and V rows move in 16-byte pieces: last dim contiguous, other strides multiples of 8.
@@ -308,8 +320,8 @@ static int decode_run(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh, c
   p.splits = (S + p.keys_per_split - 1) / p.keys_per_split;
   p.scale_log2 = (float)scale * kLog2e;
   p.part_o = static_cast<float *>(workspace);
-  p.part_ml = p.part_o + (size_t)B * Lq * H * p.splits * kHeadDim;
-  return decode_launch(p, B, Hkv, stream);
+  p.part_ml = p.part_o + (size_t)B * Lq * H * p.splits * d;
+  return decode_launch(p, d, B, Hkv, stream);
 }
 
 extern "C" int fpx_decode_attention(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
@@ -385,7 +397,7 @@ extern "C" int fpx_decode_attention_noalloc(const void *q, int64_t q_sb, int64_t
                                             void *out, int64_t o_sb, int64_t o_sl, int64_t o_sh,
                                             float *lse, fpx_stream_t stream) {
   FPX_BIND(stream);
-  if (d != kHeadDim) return FPX_ERR_UNSUPPORTED;
+  if (d != kHeadDim && d != 256) return FPX_ERR_UNSUPPORTED;
   if (!q || !k || !v || !out || B <= 0 || Lq <= 0 || S <= 0 || H <= 0 || Hkv <= 0)
     return FPX_ERR_INVALID;
   // Q, K and V rows move in 16-byte pieces: last dim contiguous, other strides multiples of 8.
@@ -412,6 +424,6 @@ extern "C" int fpx_decode_attention_noalloc(const void *q, int64_t q_sb, int64_t
   p.splits = (S + p.keys_per_split - 1) / p.keys_per_split;
   p.scale_log2 = (float)scale * kLog2e;
   p.part_o = static_cast<float *>(scratch);
-  p.part_ml = p.part_o + (size_t)B * Lq * H * p.splits * kHeadDim;
-  return decode_launch(p, B, Hkv, stream);
+  p.part_ml = p.part_o + (size_t)B * Lq * H * p.splits * d;
+  return decode_launch(p, d, B, Hkv, stream);
 }

@@ -243,6 +243,7 @@ int fpx_rope_neox_at(void *x, int64_t x_sb, int64_t x_sl, int64_t x_sh, int B, i
 int fpx_silu_mul(const void *gate_up, int64_t rows, int inter, void *out, fpx_stream_t stream);
 
 /* ---- dense decode (attention.py:178-189) --------------------------------------------- */
+/* Head dim d = 128 or 256 (the Qwen3.5 shape); at most 16 query heads per KV head. */
 
 /* Device bytes of workspace fpx_decode_attention needs. */
 size_t fpx_decode_workspace_bytes(int B, int Lq, int H, int Hkv, int S, int d);

@@ -117,3 +117,20 @@ def test_mean_methods_refuse_head_dim_256():
     q, k, v = (x.to(DEV) for x in synthetic.attention_inputs(shape, seed=1))
     with pytest.raises(RuntimeError):
         ops.prefill_attention(q, k, v, "mean_native", 0.08, SCALE)
+
+
+def test_decode_at_head_dim_256_matches_dense_softmax():
+    """The backend's decode branch (attention.py:178-189) at head dim 256: the split-K decode
+    kernel against a dense fp32 softmax, one and three query rows, 16:4 GQA."""
+    from exp3_b200 import decode
+    g = torch.Generator().manual_seed(256)
+    for lq, s_len in ((1, 4097), (3, 300)):
+        q = torch.randn(2, lq, 16, 256, generator=g).to(torch.bfloat16)
+        k = torch.randn(2, s_len, 4, 256, generator=g).to(torch.bfloat16)
+        v = torch.randn(2, s_len, 4, 256, generator=g).to(torch.bfloat16)
+        out = decode.decode_attention(q.to(DEV), k.to(DEV), v.to(DEV), SCALE).cpu().float()
+        kf = k.float().repeat_interleave(4, dim=2)
+        vf = v.float().repeat_interleave(4, dim=2)
+        w = torch.einsum("bqhd,bkhd->bhqk", q.float(), kf).mul(SCALE).softmax(-1)
+        ref = torch.einsum("bhqk,bkhd->bqhd", w, vf)
+        torch.testing.assert_close(out, ref, atol=O_TOL, rtol=0)
