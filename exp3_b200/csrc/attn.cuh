@@ -62,6 +62,7 @@ struct MeanParams {
   const __nv_bfloat16 *k, *v;
   int64_t k_sb, k_sl, k_sh, v_sb, v_sl, v_sh;
   uint8_t *choice;
+  int d;                            // head dim: 128 (0 reads as 128) or 256 (block-mean tail only)
 };
 
 // keys: 0 block means (mean_tail), 1 rescue tokens, 2 rescue tokens + remainder means.
@@ -76,6 +77,6 @@ int launch_rescue_tail_tc(const MeanParams &p, int keys, int B, int L, int tiles
 int launch_mean_tail_tc(const MeanParams &p, int B, int tiles, int heads, cudaStream_t s);
 int launch_merge(const __nv_bfloat16 *exact_out, const float *exact_lse, const float *mean_out,
                  const float *mean_lse, int64_t rows, __nv_bfloat16 *out, float *lse,
-                 cudaStream_t s);
+                 cudaStream_t s, int d = kHeadDim);
 
 }  // namespace fpx

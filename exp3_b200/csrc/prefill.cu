@@ -120,8 +120,9 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
   FPX_BIND(stream);
   if (method < 0 || method > FPX_METHOD_FP_V1_RESCUE_V2) return FPX_ERR_INVALID;
   if (block != kBlock) return FPX_ERR_UNSUPPORTED;
-  // Head dim 256 (the Qwen3.5 path, check_qwen35_math.py) runs dense and fp_v1.
-  if (d != kHeadDim && !(d == 256 && (method == FPX_METHOD_DENSE || method == FPX_METHOD_FP_V1)))
+  // Head dim 256 (the Qwen3.5 path, check_qwen35_math.py) runs dense, fp_v1 and mean_native.
+  if (d != kHeadDim && !(d == 256 && (method == FPX_METHOD_DENSE || method == FPX_METHOD_FP_V1 ||
+                                      method == FPX_METHOD_MEAN_NATIVE)))
     return FPX_ERR_UNSUPPORTED;
   if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
       !aligned16(out))
@@ -219,9 +220,11 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     mp.head_begin = head_begin; mp.tile_begin = tile_begin;
     mp.scale = (float)scale; mp.route = rv;
     mp.out = static_cast<__nv_bfloat16 *>(out); mp.o_sb = o_sb; mp.o_sl = o_sl; mp.o_sh = o_sh;
-    mp.lse = lse_out;
-    rc = get_option(kOptMeanKernel) == kMeanKernelFp32 ? launch_mean_tail(mp, kMeanMergeInPlace, tiles, heads, B, s)
-                                                       : launch_mean_tail_tc(mp, B, tiles, heads, s);
+    mp.lse = lse_out; mp.d = d;
+    // The tensor-core tail is written for head dim 128; head dim 256 takes the fp32 tail.
+    rc = (get_option(kOptMeanKernel) == kMeanKernelFp32 || d == 256)
+             ? launch_mean_tail(mp, kMeanMergeInPlace, tiles, heads, B, s)
+             : launch_mean_tail_tc(mp, B, tiles, heads, s);
   }
   if ((stages & FPX_STAGE_MEAN) && is_rescue_method(method)) {
     // attention.py:306-331: rescue tail (kernels.py:233-309), merged in place like the mean tail
@@ -302,7 +305,7 @@ extern "C" int fpx_mean_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_t 
                              fpx_stream_t stream) {
   FPX_BIND(stream);
   (void)counts;  // n_kb follows from L
-  if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
+  if ((d != kHeadDim && d != 256) || block != kBlock) return FPX_ERR_UNSUPPORTED;
   if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || !aligned16(q) || !aligned16(mean_k) ||
       !aligned16(mean_v) || !selected || !aligned16(out) || !lse)
     return FPX_ERR_INVALID;
@@ -313,7 +316,7 @@ extern "C" int fpx_mean_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_t 
   mp.mean_k = mean_k; mp.mean_v = mean_v;
   mp.L = L; mp.nb = (L + kBlock - 1) / kBlock; mp.H = H; mp.Hkv = Hkv; mp.group = H / Hkv;
   mp.head_begin = 0; mp.tile_begin = 0; mp.scale = (float)scale;
-  mp.mask = selected; mp.mean_out = out; mp.mean_lse = lse;
+  mp.mask = selected; mp.mean_out = out; mp.mean_lse = lse; mp.d = d;
   return launch_mean_tail(mp, kMeanStandalone, mp.nb, H, B, stream);
 }
 
@@ -389,10 +392,10 @@ extern "C" int fpx_merge_exact_mean(const void *exact_out, const float *exact_ls
                                     const float *mean_out, const float *mean_lse, int64_t rows,
                                     int d, void *out, float *lse, fpx_stream_t stream) {
   FPX_BIND(stream);
-  if (d != kHeadDim) return FPX_ERR_UNSUPPORTED;
+  if (d != kHeadDim && d != 256) return FPX_ERR_UNSUPPORTED;
   if (rows < 0 || !aligned16(exact_out) || !exact_lse || !aligned16(mean_out) || !mean_lse ||
       !aligned16(out) || !lse)
     return FPX_ERR_INVALID;
   return launch_merge(static_cast<const __nv_bfloat16 *>(exact_out), exact_lse, mean_out, mean_lse,
-                      rows, static_cast<__nv_bfloat16 *>(out), lse, stream);
+                      rows, static_cast<__nv_bfloat16 *>(out), lse, stream, d);
 }

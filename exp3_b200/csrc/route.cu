@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(D) block_stats_kernel(StatsParams p) {
   const int64_t o = (((int64_t)b * p.nb + blk) * p.Hkv + kvh) * D + c;
   if (kBf16Mean) p.mean_bf16[o] = __float2bfloat16_rn(__fdiv_rn(sk, fn));
   if (kDesc) {
-    __shared__ float red[4];
+    __shared__ float red[D / 32];
     const float mk = __fdiv_rn(sk, fn);
     const float mv = __fdiv_rn(sv, fn);
     p.mean_k[o] = mk;
@@ -69,9 +69,13 @@ int launch_block_stats(const StatsParams &p, int blocks, int kv_count, int B, bo
                        bool desc, cudaStream_t s) {
   if (blocks <= 0 || kv_count <= 0) return FPX_OK;
   dim3 grid(blocks, kv_count, B);
-  if (p.d == 256) {  // head dim 256: the V1 block mean only (fp_v1, check_qwen35_math.py:46-51)
-    if (desc || !bf16_mean) return FPX_ERR_UNSUPPORTED;
-    block_stats_kernel<true, false, 256><<<grid, 256, 0, s>>>(p);
+  if (p.d == 256) {  // head dim 256 (check_qwen35_math.py): one thread per dimension
+    if (bf16_mean && desc)
+      block_stats_kernel<true, true, 256><<<grid, 256, 0, s>>>(p);
+    else if (bf16_mean)
+      block_stats_kernel<true, false, 256><<<grid, 256, 0, s>>>(p);
+    else if (desc)
+      block_stats_kernel<false, true, 256><<<grid, 256, 0, s>>>(p);
     FPX_CHECK_LAUNCH();
     return FPX_OK;
   }
@@ -656,8 +660,9 @@ extern "C" int fpx_block_descriptors(const void *k, int64_t k_sb, int64_t k_sl, 
   FPX_BIND(stream);
   if (!k || !v || !mean_k || !mean_v || !var_k || !sigma_v || B <= 0 || L <= 0 || Hkv <= 0)
     return FPX_ERR_INVALID;
-  if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
+  if ((d != kHeadDim && d != 256) || block != kBlock) return FPX_ERR_UNSUPPORTED;
   StatsParams p{};
+  p.d = d;
   p.k = static_cast<const __nv_bfloat16 *>(k);
   p.k_sb = k_sb; p.k_sl = k_sl; p.k_sh = k_sh;
   p.v = static_cast<const __nv_bfloat16 *>(v);

@@ -3,7 +3,8 @@
 The reference's fp_v1 path at d = 256 through the C ABI: the bf16 block mean, the V1 scores and
 selection against the reference's golden vectors, the tcgen05 d = 256 exact kernel in the
 reference layout (all causal blocks, and a fixed mask), and the fused fp_v1 / dense prefill
-against the oracle. Bars as for d = 128: masks bit-exact outside the 1e-6 band, O 2e-2, LSE 1e-3.
+against the oracle; also mean_native (descriptors, the block-mean tail and the merge) and decode
+at d = 256. Bars as for d = 128: masks bit-exact outside the 1e-6 band, O 2e-2, LSE 1e-3.
 """
 
 import pytest
@@ -112,11 +113,45 @@ def test_backend_fp_v1_at_head_dim_256():
     torch.testing.assert_close(out.cpu().float(), ref, atol=0.03, rtol=0.03)
 
 
-def test_mean_methods_refuse_head_dim_256():
+def test_fused_mean_native_at_head_dim_256():
+    """mean_native on the Qwen3.5 shape: V1 routing, the d = 256 exact kernel, the fp32
+    block-mean tail (four threads per row) merged in place; structured inputs so tails exist."""
+    shape = synthetic.LayerShape(1, 2177, 16, 4, 256)
+    q, k, v = synthetic.attention_inputs(shape, seed=43, needles=4, structured_sigma=0.5)
+    blocks = oracle.num_blocks(2177)
+    sel = _fused_vs_oracle("mean_native", q, k, v, 0.08, list(range(blocks)))
+    assert int(sel.sum()) < 16 * blocks * (blocks + 1) // 2  # tails exist
+
+
+def test_descriptors_mean_tail_and_merge_ops_at_head_dim_256():
+    from exp3_b200 import kernels
+    shape = synthetic.LayerShape(1, 385, 8, 2, 256)
+    q, k, v = synthetic.attention_inputs(shape, seed=44, needles=1)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    desc = kernels.block_descriptors(kd, vd)
+    ref = oracle.block_descriptors(k.float(), v.float())
+    for name in ("mean_k", "mean_v", "var_k", "sigma_v"):
+        torch.testing.assert_close(getattr(desc, name).cpu(), getattr(ref, name), atol=2e-6, rtol=1e-5)
+    selected = oracle.protected_selection(torch.zeros(1, 4, 4, 8), 0.0, 2, 4, 2)
+    selected[:, 3, 1, ::2] = False
+    selected[:, 3, 0, 1::3] = False
+    mo, ml = kernels.mean_tail(qd, desc, selected.to(DEV), SCALE)
+    mo_ref, ml_ref = oracle.mean_tail(q.float(), ref, selected, SCALE)
+    torch.testing.assert_close(ml.cpu(), ml_ref, atol=LSE_TOL, rtol=0)
+    torch.testing.assert_close(mo.cpu(), mo_ref, atol=O_TOL, rtol=0)
+    idx, cnt = oracle.indices_from_mask(selected)
+    eo, el = upstream.exact_attention(qd, kd, vd, idx.to(DEV), cnt.to(DEV), SCALE)
+    merged, merged_lse = kernels.merge_exact_mean(eo, el, mo, ml)
+    m_ref, ml2_ref = oracle.merge_exact_mean(eo.cpu(), el.cpu(), mo_ref, ml_ref)
+    torch.testing.assert_close(merged.cpu().float(), m_ref.float(), atol=O_TOL, rtol=0)
+    torch.testing.assert_close(merged_lse.cpu(), ml2_ref, atol=LSE_TOL, rtol=0)
+
+
+def test_new_selectors_refuse_head_dim_256():
     shape = synthetic.LayerShape(1, 256, 4, 1, 256)
     q, k, v = (x.to(DEV) for x in synthetic.attention_inputs(shape, seed=1))
     with pytest.raises(RuntimeError):
-        ops.prefill_attention(q, k, v, "mean_native", 0.08, SCALE)
+        ops.prefill_attention(q, k, v, "cgf_mean", 0.08, SCALE)
 
 
 def test_decode_at_head_dim_256_matches_dense_softmax():
