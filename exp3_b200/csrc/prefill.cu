@@ -120,10 +120,8 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
   FPX_BIND(stream);
   if (method < 0 || method > FPX_METHOD_FP_V1_RESCUE_V2) return FPX_ERR_INVALID;
   if (block != kBlock) return FPX_ERR_UNSUPPORTED;
-  // Head dim 256 (the Qwen3.5 path, check_qwen35_math.py) runs dense, fp_v1 and mean_native.
-  if (d != kHeadDim && !(d == 256 && (method == FPX_METHOD_DENSE || method == FPX_METHOD_FP_V1 ||
-                                      method == FPX_METHOD_MEAN_NATIVE)))
-    return FPX_ERR_UNSUPPORTED;
+  // Head dim 256 (the Qwen3.5 path, check_qwen35_math.py) runs every method but the rescue ones.
+  if (d != kHeadDim && !(d == 256 && !is_rescue_method(method))) return FPX_ERR_UNSUPPORTED;
   if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
       !aligned16(out))
     return FPX_ERR_INVALID;
@@ -188,8 +186,11 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
         sp.scale = (float)scale; sp.scale2 = (float)(scale * scale);
         sp.scores = nullptr; sp.sel = sel;
         sp.mk_hi = ws.mkh; sp.mk_lo = ws.mkl; sp.vk_hi = ws.vkh; sp.vk_lo = ws.vkl;
-        rc = get_option(kOptSelectorKernel) == kSelectorKernelFp32 ? launch_selector_route(sp, method, tiles, heads, B, s)
-                                                                   : launch_selector_route_tc(sp, method, tiles, heads, B, s);
+        sp.d = d;
+        // The tensor-core selector kernel is written for head dim 128; 256 takes the fp32 one.
+        rc = (get_option(kOptSelectorKernel) == kSelectorKernelFp32 || d == 256)
+                 ? launch_selector_route(sp, method, tiles, heads, B, s)
+                 : launch_selector_route_tc(sp, method, tiles, heads, B, s);
       }
     }
     if (rc) return rc;

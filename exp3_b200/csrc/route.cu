@@ -299,16 +299,16 @@ int launch_v1_route(const V1Params &p, int tiles, int heads, int B, cudaStream_t
 // reduced across rows in a fixed order (warp shuffles, then the 4 warps in sequence).
 constexpr int kSelChunk = 32;
 
-template <int kSel>  // 0 mean_balanced, 1 cgf_mean, 2 dispersion_mean
+template <int kSel, int D = kHeadDim>  // kSel: 0 mean_balanced, 1 cgf_mean, 2 dispersion_mean
 __global__ void __launch_bounds__(128) selector_route_kernel(SelParams p) {
   const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);
   const int h = p.head_begin + blockIdx.y;
   const int b = blockIdx.z;
   const int kvh = h / p.group;
   extern __shared__ __align__(16) uint8_t smem[];
-  float *smk = reinterpret_cast<float *>(smem);          // [32][128]
-  float *svk = smk + kSelChunk * kHeadDim;                // [32][128]
-  float *part = svk + kSelChunk * kHeadDim;               // [4][32]
+  float *smk = reinterpret_cast<float *>(smem);          // [32][D]
+  float *svk = smk + kSelChunk * D;                       // [32][D]
+  float *part = svk + kSelChunk * D;                      // [4][32]
   float *sc = part + 4 * kSelChunk;                       // [nb]
   int *scratch = reinterpret_cast<int *>(sc + p.nb);      // [4]
   float *red = reinterpret_cast<float *>(scratch + 4);    // [4]
@@ -318,29 +318,29 @@ __global__ void __launch_bounds__(128) selector_route_kernel(SelParams p) {
   const int rows = min(kBlock, p.L - t * kBlock);
   const bool valid = tid < rows;
   const int pos = t * kBlock + min(tid, rows - 1);
-  uint32_t qv[64];
+  uint32_t qv[D / 2];
   {
     const uint4 *src = reinterpret_cast<const uint4 *>(p.q + b * p.q_sb + (int64_t)pos * p.q_sl +
                                                        h * p.q_sh);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < D / 8; ++i) {
       const uint4 u = src[i];
       qv[4 * i] = u.x; qv[4 * i + 1] = u.y; qv[4 * i + 2] = u.z; qv[4 * i + 3] = u.w;
     }
   }
-  const float *mk_base = p.mean_k + ((int64_t)b * p.nb * p.Hkv + kvh) * kHeadDim;
-  const float *vk_base = p.var_k + ((int64_t)b * p.nb * p.Hkv + kvh) * kHeadDim;
-  const int64_t dstride = (int64_t)p.Hkv * kHeadDim;
+  const float *mk_base = p.mean_k + ((int64_t)b * p.nb * p.Hkv + kvh) * D;
+  const float *vk_base = p.var_k + ((int64_t)b * p.nb * p.Hkv + kvh) * D;
+  const int64_t dstride = (int64_t)p.Hkv * D;
   for (int kb = tid; kb < p.nb; kb += 128) sc[kb] = 0.f;
 
   auto stage = [&](int c0, int cn) {
     __syncthreads();
-    for (int i = tid; i < cn * 32; i += 128) {
-      const int j = i >> 5, q4 = i & 31;
-      reinterpret_cast<float4 *>(smk + j * kHeadDim)[q4] =
+    for (int i = tid; i < cn * (D / 4); i += 128) {
+      const int j = i / (D / 4), q4 = i % (D / 4);
+      reinterpret_cast<float4 *>(smk + j * D)[q4] =
           reinterpret_cast<const float4 *>(mk_base + (c0 + j) * dstride)[q4];
       if (kSel > 0)
-        reinterpret_cast<float4 *>(svk + j * kHeadDim)[q4] =
+        reinterpret_cast<float4 *>(svk + j * D)[q4] =
             reinterpret_cast<const float4 *>(vk_base + (c0 + j) * dstride)[q4];
     }
     if (tid < cn) {
@@ -352,11 +352,11 @@ __global__ void __launch_bounds__(128) selector_route_kernel(SelParams p) {
   };
   // Logit of block j of the staged chunk (and sqrt(u) for dispersion).
   auto logit = [&](int j, float &disp) -> float {
-    const float4 *m4 = reinterpret_cast<const float4 *>(smk + j * kHeadDim);
-    const float4 *v4 = reinterpret_cast<const float4 *>(svk + j * kHeadDim);
+    const float4 *m4 = reinterpret_cast<const float4 *>(smk + j * D);
+    const float4 *v4 = reinterpret_cast<const float4 *>(svk + j * D);
     float dot = 0.f, udot = 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < D / 4; ++i) {
       const float2 qa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qv[2 * i]));
       const float2 qb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qv[2 * i + 1]));
       const float4 m = m4[i];
@@ -421,30 +421,32 @@ __global__ void __launch_bounds__(128) selector_route_kernel(SelParams p) {
   if (p.sel.route.lists) select_and_emit<128, true>(sc, smax, p.sel, b, h, t, scratch);
 }
 
-size_t selector_route_smem(int nb) {
-  return (size_t)2 * kSelChunk * kHeadDim * 4 + 4 * kSelChunk * 4 + (size_t)nb * 4 + 32 +
-         2 * kSelChunk * 4 + 64;
+size_t selector_route_smem(int nb, int d) {
+  return (size_t)2 * kSelChunk * d * 4 + 4 * kSelChunk * 4 + (size_t)nb * 4 + 32 + 2 * kSelChunk * 4 + 64;
 }
 
 int launch_selector_route(const SelParams &p, int selector, int tiles, int heads, int B,
                           cudaStream_t s) {
   if (tiles <= 0 || heads <= 0) return FPX_OK;
-  const size_t smem = selector_route_smem(p.nb);
+  const int d = p.d == 256 ? 256 : kHeadDim;
+  const size_t smem = selector_route_smem(p.nb, d);
+  if (smem > 200 * 1024) return FPX_ERR_UNSUPPORTED;
   dim3 grid(tiles, heads, B);
-#define FPX_SEL_LAUNCH(K)                                                                    \
-  do {                                                                                       \
-    cudaFuncSetAttribute(selector_route_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                         (int)smem);                                                         \
-    selector_route_kernel<K><<<grid, 128, smem, s>>>(p);                                     \
+#define FPX_SEL_LAUNCH(K, DD)                                                                    \
+  do {                                                                                           \
+    cudaFuncSetAttribute(selector_route_kernel<K, DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                         (int)smem);                                                             \
+    selector_route_kernel<K, DD><<<grid, 128, smem, s>>>(p);                                     \
   } while (0)
-  if (selector == FPX_METHOD_MEAN_BALANCED)
-    FPX_SEL_LAUNCH(0);
-  else if (selector == FPX_METHOD_CGF_MEAN)
-    FPX_SEL_LAUNCH(1);
-  else if (selector == FPX_METHOD_DISPERSION_MEAN)
-    FPX_SEL_LAUNCH(2);
-  else
+  if (selector == FPX_METHOD_MEAN_BALANCED) {
+    if (d == 256) FPX_SEL_LAUNCH(0, 256); else FPX_SEL_LAUNCH(0, kHeadDim);
+  } else if (selector == FPX_METHOD_CGF_MEAN) {
+    if (d == 256) FPX_SEL_LAUNCH(1, 256); else FPX_SEL_LAUNCH(1, kHeadDim);
+  } else if (selector == FPX_METHOD_DISPERSION_MEAN) {
+    if (d == 256) FPX_SEL_LAUNCH(2, 256); else FPX_SEL_LAUNCH(2, kHeadDim);
+  } else {
     return FPX_ERR_INVALID;
+  }
 #undef FPX_SEL_LAUNCH
   FPX_CHECK_LAUNCH();
   return FPX_OK;
@@ -701,7 +703,7 @@ extern "C" int fpx_selector_scores(const void *q, int64_t q_sb, int64_t q_sl, in
   if (!ptr_ok(q) || !mean_k || !var_k || !sigma_v || !scores || B <= 0 || L <= 0 || H <= 0 ||
       Hkv <= 0)
     return FPX_ERR_INVALID;
-  if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
+  if ((d != kHeadDim && d != 256) || block != kBlock) return FPX_ERR_UNSUPPORTED;
   if (selector < FPX_METHOD_MEAN_BALANCED || selector > FPX_METHOD_DISPERSION_MEAN)
     return FPX_ERR_INVALID;
   if (H % Hkv || !stride_ok(q_sb, q_sl, q_sh)) return FPX_ERR_SHAPE;
@@ -712,6 +714,7 @@ extern "C" int fpx_selector_scores(const void *q, int64_t q_sb, int64_t q_sl, in
   p.L = L; p.nb = (L + kBlock - 1) / kBlock; p.H = H; p.Hkv = Hkv; p.group = H / Hkv;
   p.scale = (float)scale; p.scale2 = (float)(scale * scale);
   p.scores = scores;
+  p.d = d;
   return launch_selector_route(p, selector, p.nb, H, B, stream);
 }
 

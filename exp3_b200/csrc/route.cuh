@@ -46,6 +46,7 @@ struct SelParams {
   float scale, scale2;          // fp32(scale), fp32(scale * scale)
   float *scores;
   SelectArgs sel;
+  int d;                        // head dim: 128 (0 reads as 128) or 256 (the fp32 kernel only)
 };
 
 struct ColumnSelectParams {

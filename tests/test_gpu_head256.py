@@ -147,11 +147,34 @@ def test_descriptors_mean_tail_and_merge_ops_at_head_dim_256():
     torch.testing.assert_close(merged_lse.cpu(), ml2_ref, atol=LSE_TOL, rtol=0)
 
 
-def test_new_selectors_refuse_head_dim_256():
+@pytest.mark.parametrize("method", ["mean_balanced", "cgf_mean", "dispersion_mean"])
+def test_fused_new_selectors_at_head_dim_256(method):
+    """The new selectors on the Qwen3.5 shape: fp32 selector routing (q row in registers, 256
+    dimensions), the d = 256 exact kernel and the fp32 block-mean tail, against the oracle.
+    (Log-normal K row norms are exercised at d = 128 on the config-5 shape; at d = 256 they push
+    single outputs near 2.0, where the bar of 2e-2 is three bf16 steps.)"""
+    shape = synthetic.LayerShape(1, 1409, 16, 4, 256)  # 12 blocks, the last with one row
+    q, k, v = synthetic.attention_inputs(shape, seed=45, needles=2, structured_sigma=0.5)
+    _fused_vs_oracle(method, q, k, v, 0.08, list(range(oracle.num_blocks(1409))))
+
+
+def test_selector_scores_op_at_head_dim_256():
+    from exp3_b200 import kernels
+    shape = synthetic.LayerShape(1, 385, 8, 2, 256)
+    q, k, v = synthetic.attention_inputs(shape, seed=46, needles=1)
+    desc = kernels.block_descriptors(k.to(DEV), v.to(DEV))
+    ref_desc = oracle.block_descriptors(k.float(), v.float())
+    for selector in oracle.SELECTORS:
+        got = kernels.selector_scores(q.to(DEV), desc, SCALE, selector).cpu()
+        ref = oracle.selector_scores(q.float(), ref_desc, SCALE, selector)
+        torch.testing.assert_close(got, ref, atol=2e-6, rtol=1e-5)
+
+
+def test_rescue_methods_refuse_head_dim_256():
     shape = synthetic.LayerShape(1, 256, 4, 1, 256)
     q, k, v = (x.to(DEV) for x in synthetic.attention_inputs(shape, seed=1))
     with pytest.raises(RuntimeError):
-        ops.prefill_attention(q, k, v, "cgf_mean", 0.08, SCALE)
+        ops.prefill_attention(q, k, v, "fp_v1_rescue", 0.08, SCALE)
 
 
 def test_decode_at_head_dim_256_matches_dense_softmax():
