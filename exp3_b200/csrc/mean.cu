@@ -222,10 +222,16 @@ int launch_mean_tail(const MeanParams &p, int mode, int tiles, int heads, int B,
   if (keys != 0 && (!p.choice || !p.k || !p.v)) return FPX_ERR_INVALID;
   dim3 grid(tiles, heads, B);
   const bool merge = mode == kMeanMergeInPlace;
-  if (d == 256) {  // head dim 256: the block-mean tail (mean_native)
-    if (keys != 0) return FPX_ERR_UNSUPPORTED;
-    merge ? launch_tail_variant<kMeanMergeInPlace, 0, 256>(p, grid, smem, s)
-          : launch_tail_variant<kMeanStandalone, 0, 256>(p, grid, smem, s);
+  if (d == 256) {  // head dim 256: block-mean and rescue tails on the fp32 kernel
+    switch (keys) {
+      case 0: merge ? launch_tail_variant<kMeanMergeInPlace, 0, 256>(p, grid, smem, s)
+                    : launch_tail_variant<kMeanStandalone, 0, 256>(p, grid, smem, s); break;
+      case 1: merge ? launch_tail_variant<kMeanMergeInPlace, 1, 256>(p, grid, smem, s)
+                    : launch_tail_variant<kMeanStandalone, 1, 256>(p, grid, smem, s); break;
+      case 2: merge ? launch_tail_variant<kMeanMergeInPlace, 2, 256>(p, grid, smem, s)
+                    : launch_tail_variant<kMeanStandalone, 2, 256>(p, grid, smem, s); break;
+      default: return FPX_ERR_INVALID;
+    }
     FPX_CHECK_LAUNCH();
     return FPX_OK;
   }

@@ -120,8 +120,8 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
   FPX_BIND(stream);
   if (method < 0 || method > FPX_METHOD_FP_V1_RESCUE_V2) return FPX_ERR_INVALID;
   if (block != kBlock) return FPX_ERR_UNSUPPORTED;
-  // Head dim 256 (the Qwen3.5 path, check_qwen35_math.py) runs every method but the rescue ones.
-  if (d != kHeadDim && !(d == 256 && !is_rescue_method(method))) return FPX_ERR_UNSUPPORTED;
+  // Head dim 128, or 256 (the Qwen3.5 path, check_qwen35_math.py).
+  if (d != kHeadDim && d != 256) return FPX_ERR_UNSUPPORTED;
   if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
       !aligned16(out))
     return FPX_ERR_INVALID;
@@ -238,12 +238,14 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     mp.head_begin = head_begin; mp.tile_begin = tile_begin;
     mp.scale = (float)scale; mp.route = rv;
     mp.out = static_cast<__nv_bfloat16 *>(out); mp.o_sb = o_sb; mp.o_sl = o_sl; mp.o_sh = o_sh;
-    mp.lse = lse_out;
+    mp.lse = lse_out; mp.d = d;
     rc = launch_rescue_choice(mp, kMeanMergeInPlace, tiles, kv_count, B, s);
     if (rc) return rc;
     const int keys = method == FPX_METHOD_FP_V1_RESCUE_V2 ? 2 : 1;
-    rc = get_option(kOptMeanKernel) == kMeanKernelFp32 ? launch_mean_tail(mp, kMeanMergeInPlace, tiles, heads, B, s, keys)
-                                                       : launch_rescue_tail_tc(mp, keys, B, L, tiles, heads, s);
+    // The tensor-core rescue tail is written for head dim 128; 256 takes the fp32 tail.
+    rc = (get_option(kOptMeanKernel) == kMeanKernelFp32 || d == 256)
+             ? launch_mean_tail(mp, kMeanMergeInPlace, tiles, heads, B, s, keys)
+             : launch_rescue_tail_tc(mp, keys, B, L, tiles, heads, s);
   }
   return rc;
 }
@@ -327,9 +329,9 @@ struct RescueWorkspace {
   float *mk, *mv, *vk, *sv;
   size_t bytes;
 };
-static RescueWorkspace carve_rescue(void *base, int B, int L, int H, int Hkv) {
+static RescueWorkspace carve_rescue(void *base, int B, int L, int H, int Hkv, int d = kHeadDim) {
   const int64_t nb = (L + kBlock - 1) / kBlock;
-  const size_t desc = (size_t)B * nb * Hkv * kHeadDim;
+  const size_t desc = (size_t)B * nb * Hkv * d;
   RescueWorkspace w{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -348,8 +350,8 @@ static RescueWorkspace carve_rescue(void *base, int B, int L, int H, int Hkv) {
 }  // namespace fpx
 
 extern "C" size_t fpx_rescue_tail_workspace_bytes(int B, int L, int H, int Hkv, int d, int block) {
-  if (d != kHeadDim || block != kBlock || B <= 0 || L <= 0 || H <= 0 || Hkv <= 0) return 0;
-  return carve_rescue(nullptr, B, L, H, Hkv).bytes;
+  if ((d != kHeadDim && d != 256) || block != kBlock || B <= 0 || L <= 0 || H <= 0 || Hkv <= 0) return 0;
+  return carve_rescue(nullptr, B, L, H, Hkv, d).bytes;
 }
 
 extern "C" int fpx_rescue_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
@@ -359,20 +361,20 @@ extern "C" int fpx_rescue_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_
                                double scale, int remainder, float *out, float *lse, void *workspace,
                                size_t workspace_bytes, fpx_stream_t stream) {
   FPX_BIND(stream);
-  if (d != kHeadDim || block != kBlock) return FPX_ERR_UNSUPPORTED;
+  if ((d != kHeadDim && d != 256) || block != kBlock) return FPX_ERR_UNSUPPORTED;
   if (B <= 0 || L <= 0 || H <= 0 || Hkv <= 0 || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
       !selected || !aligned16(out) || !lse)
     return FPX_ERR_INVALID;
   if (H % Hkv || !strides_ok(q_sb, q_sl, q_sh) || !strides_ok(k_sb, k_sl, k_sh) || !strides_ok(v_sb, v_sl, v_sh))
     return FPX_ERR_SHAPE;
-  const RescueWorkspace ws = carve_rescue(workspace, B, L, H, Hkv);
+  const RescueWorkspace ws = carve_rescue(workspace, B, L, H, Hkv, d);
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) || workspace_bytes < ws.bytes)
     return FPX_ERR_WORKSPACE;
   const int nb = (L + kBlock - 1) / kBlock;
   StatsParams st{};
   st.k = static_cast<const __nv_bfloat16 *>(k); st.k_sb = k_sb; st.k_sl = k_sl; st.k_sh = k_sh;
   st.v = static_cast<const __nv_bfloat16 *>(v); st.v_sb = v_sb; st.v_sl = v_sl; st.v_sh = v_sh;
-  st.L = L; st.nb = nb; st.Hkv = Hkv; st.kv_begin = 0;
+  st.L = L; st.nb = nb; st.Hkv = Hkv; st.kv_begin = 0; st.d = d;
   st.mean_k = ws.mk; st.mean_v = ws.mv; st.var_k = ws.vk; st.sigma_v = ws.sv;
   int rc = launch_block_stats(st, nb, Hkv, B, false, true, stream);
   if (rc) return rc;
@@ -383,7 +385,7 @@ extern "C" int fpx_rescue_tail(const void *q, int64_t q_sb, int64_t q_sl, int64_
   mp.mean_k = ws.mk; mp.mean_v = ws.mv; mp.choice = ws.choice;
   mp.L = L; mp.nb = nb; mp.H = H; mp.Hkv = Hkv; mp.group = H / Hkv;
   mp.head_begin = 0; mp.tile_begin = 0; mp.scale = (float)scale;
-  mp.mask = selected; mp.mean_out = out; mp.mean_lse = lse;
+  mp.mask = selected; mp.mean_out = out; mp.mean_lse = lse; mp.d = d;
   rc = launch_rescue_choice(mp, kMeanStandalone, nb, Hkv, B, stream);
   if (rc) return rc;
   return launch_mean_tail(mp, kMeanStandalone, nb, H, B, stream, remainder ? 2 : 1);

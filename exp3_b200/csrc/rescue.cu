@@ -20,8 +20,8 @@ constexpr int kRescueMaxGroup = 16;
 constexpr int kRescueSplits = 4;
 constexpr int kChoiceThreads = 256;
 
-template <int kMode>
-__global__ void __launch_bounds__(256, 2) rescue_choice_kernel(MeanParams p) {
+template <int kMode, int D = kHeadDim>
+__global__ void __launch_bounds__(256, D == kHeadDim ? 2 : 1) rescue_choice_kernel(MeanParams p) {
   const int t = p.tile_begin + blockIdx.x;
   const int kvh = p.head_begin / p.group + blockIdx.y;
   const int b = blockIdx.z / kRescueSplits;
@@ -29,9 +29,9 @@ __global__ void __launch_bounds__(256, 2) rescue_choice_kernel(MeanParams p) {
   const int G = p.group;
   if (t == 0) return;  // tile 0 has no earlier block
   extern __shared__ __align__(16) uint8_t smem[];
-  float *qm = reinterpret_cast<float *>(smem);                                 // [G][128]
-  float *part = qm + G * kHeadDim;                                             // [8][128]
-  float *red_v = part + 8 * kHeadDim;                                          // [8][G]
+  float *qm = reinterpret_cast<float *>(smem);                                 // [G][D]
+  float *part = qm + G * D;                                                    // [8][D]
+  float *red_v = part + 8 * D;                                                 // [8][G]
   int *red_i = reinterpret_cast<int *>(red_v + 8 * G);                         // [8][G]
   const int words = (p.nb + 31) / 32;
   uint32_t *bits = reinterpret_cast<uint32_t *>(red_i + 8 * G);                // [G][words]
@@ -71,57 +71,60 @@ __global__ void __launch_bounds__(256, 2) rescue_choice_kernel(MeanParams p) {
   __syncthreads();
   if (split >= nu) return;  // nothing for this CTA of the split (uniform)
   // Query means (kernels.py:278-279): fp32 sums over the valid rows, then divided by the count.
-  // Warp w sums rows w, w + 8, ... for dimensions 4 lane .. 4 lane + 3; the eight partial sums
+  // Warp w sums rows w, w + 8, ... for dimensions 4 lane + 128 c .. + 3; the eight partial sums
   // are added in warp order.
   const int rows = min(kBlock, p.L - t * kBlock);
   for (int g = 0; g < G; ++g) {
     const int h = kvh * G + g;
-    const __nv_bfloat16 *src = p.q + b * p.q_sb + (int64_t)t * kBlock * p.q_sl + h * p.q_sh + 4 * lane;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int c = 0; c < D / 128; ++c) {
+      const __nv_bfloat16 *src = p.q + b * p.q_sb + (int64_t)t * kBlock * p.q_sl + h * p.q_sh + 4 * lane + 128 * c;
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll 4
-    for (int r = warp; r < rows; r += 8) {
-      const uint2 u = *reinterpret_cast<const uint2 *>(src + (int64_t)r * p.q_sl);
-      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
-      const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
-      s0 += a.x; s1 += a.y; s2 += c.x; s3 += c.y;
+      for (int r = warp; r < rows; r += 8) {
+        const uint2 u = *reinterpret_cast<const uint2 *>(src + (int64_t)r * p.q_sl);
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
+        const float2 cc = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
+        s0 += a.x; s1 += a.y; s2 += cc.x; s3 += cc.y;
+      }
+      *reinterpret_cast<float4 *>(part + warp * D + 4 * lane + 128 * c) = make_float4(s0, s1, s2, s3);
     }
-    *reinterpret_cast<float4 *>(part + warp * kHeadDim + 4 * lane) = make_float4(s0, s1, s2, s3);
     __syncthreads();
-    if (tid < kHeadDim) {
+    if (tid < D) {
       float s = 0.f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) s += part[w * kHeadDim + tid];
-      qm[g * kHeadDim + tid] = s / (float)rows;
+      for (int w = 0; w < 8; ++w) s += part[w * D + tid];
+      qm[g * D + tid] = s / (float)rows;
     }
     __syncthreads();
   }
 
-  // Thread pair (2 j, 2 j + 1) holds token j's key row, 64 dimensions each.
+  // Thread pair (2 j, 2 j + 1) holds token j's key row, D / 2 dimensions each.
   const int tok = tid >> 1, half = tid & 1;
   uint8_t *choice = p.choice;
-  auto load_row = [&](int kb, uint4 (&dst)[8]) {
+  auto load_row = [&](int kb, uint4 (&dst)[D / 16]) {
     const uint4 *row = reinterpret_cast<const uint4 *>(p.k + b * p.k_sb + ((int64_t)kb * kBlock + tok) * p.k_sl +
-                                                       kvh * p.k_sh + 64 * half);
+                                                       kvh * p.k_sh + (D / 2) * half);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) dst[i] = row[i];
+    for (int i = 0; i < D / 16; ++i) dst[i] = row[i];
   };
-  uint4 nxt[8];
+  uint4 nxt[D / 16];
   load_row(ulist[split], nxt);
   for (int e = split; e < nu; e += kRescueSplits) {
     const int kb = ulist[e];
     // The next block's half row is requested before this block's dots.
-    uint32_t kr[32];
+    uint32_t kr[D / 4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < D / 16; ++i) {
       kr[4 * i] = nxt[i].x; kr[4 * i + 1] = nxt[i].y; kr[4 * i + 2] = nxt[i].z; kr[4 * i + 3] = nxt[i].w;
     }
     if (e + kRescueSplits < nu) load_row(ulist[e + kRescueSplits], nxt);
     for (int g = 0; g < G; ++g) {
       if (!((bits[g * words + (kb >> 5)] >> (kb & 31)) & 1u)) continue;  // uniform per head
-      const float4 *m4 = reinterpret_cast<const float4 *>(qm + g * kHeadDim + 64 * half);
+      const float4 *m4 = reinterpret_cast<const float4 *>(qm + g * D + (D / 2) * half);
       float dot = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < D / 8; ++i) {
         const float4 m = m4[i];
         const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[2 * i]));
         const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[2 * i + 1]));
@@ -170,19 +173,22 @@ __global__ void __launch_bounds__(256, 2) rescue_choice_kernel(MeanParams p) {
 int launch_rescue_choice(const MeanParams &p, int mode, int tiles, int kv_count, int B, cudaStream_t s) {
   if (tiles <= 0 || kv_count <= 0) return FPX_OK;
   if (p.group > kRescueMaxGroup || !p.choice || !p.k) return FPX_ERR_UNSUPPORTED;
-  const size_t smem = (size_t)p.group * kHeadDim * 4 + 8 * kHeadDim * 4 + 16 * p.group * 4 +
+  const int d = p.d == 256 ? 256 : kHeadDim;
+  const size_t smem = (size_t)p.group * d * 4 + 8 * d * 4 + 16 * p.group * 4 +
                       (size_t)p.group * ((p.nb + 31) / 32) * 4 + (size_t)((p.nb + 1) & ~1) * 2 + 32;
   if (smem > 200 * 1024) return FPX_ERR_UNSUPPORTED;
   const dim3 grid(tiles, kv_count, B * kRescueSplits);
+#define FPX_CHOICE_LAUNCH(MODE, DD)                                                                     \
+  do {                                                                                                  \
+    cudaFuncSetAttribute(rescue_choice_kernel<MODE, DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    rescue_choice_kernel<MODE, DD><<<grid, kChoiceThreads, smem, s>>>(p);                               \
+  } while (0)
   if (mode == kMeanMergeInPlace) {
-    cudaFuncSetAttribute(rescue_choice_kernel<kMeanMergeInPlace>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    rescue_choice_kernel<kMeanMergeInPlace><<<grid, kChoiceThreads, smem, s>>>(p);
+    if (d == 256) FPX_CHOICE_LAUNCH(kMeanMergeInPlace, 256); else FPX_CHOICE_LAUNCH(kMeanMergeInPlace, kHeadDim);
   } else {
-    cudaFuncSetAttribute(rescue_choice_kernel<kMeanStandalone>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    rescue_choice_kernel<kMeanStandalone><<<grid, kChoiceThreads, smem, s>>>(p);
+    if (d == 256) FPX_CHOICE_LAUNCH(kMeanStandalone, 256); else FPX_CHOICE_LAUNCH(kMeanStandalone, kHeadDim);
   }
+#undef FPX_CHOICE_LAUNCH
   FPX_CHECK_LAUNCH();
   return FPX_OK;
 }

@@ -83,10 +83,9 @@ int fpx_set_option(int key, int value);
 int fpx_device_error(int *code, int reset);
 
 /* ---- routing ------------------------------------------------------------------------ */
-/* Head dim d = 128 for every entry point; d = 256 (the Qwen3.5 shape) for block_mean_k,
- * block_descriptors, v1_scores, selector_scores, exact_attention, mean_tail, merge_exact_mean,
- * the decode entry points, and prefill_attention / prefill_export_routing with every method
- * but the rescue ones (those, and rescue_tail, return FPX_ERR_UNSUPPORTED at 256). */
+/* Head dim d = 128 or 256 (the Qwen3.5 shape) for every attention entry point: routing,
+ * descriptors, selectors, exact attention, the tails, the merge, prefill_attention with every
+ * method, and decode. (At 256 the selector routing and the tails run on fp32 kernels.) */
 
 /* upstream:420-442 block_mean_k (compute_mean_vector upstream:27-69): bf16 mean of the
  * valid K rows of each (block, KV head) -> mean_k bf16 [B, nb, Hkv, d] contiguous.

@@ -170,11 +170,26 @@ def test_selector_scores_op_at_head_dim_256():
         torch.testing.assert_close(got, ref, atol=2e-6, rtol=1e-5)
 
 
-def test_rescue_methods_refuse_head_dim_256():
-    shape = synthetic.LayerShape(1, 256, 4, 1, 256)
-    q, k, v = (x.to(DEV) for x in synthetic.attention_inputs(shape, seed=1))
-    with pytest.raises(RuntimeError):
-        ops.prefill_attention(q, k, v, "fp_v1_rescue", 0.08, SCALE)
+@pytest.mark.parametrize("method", ["fp_v1_rescue", "fp_v1_rescue_v2"])
+def test_fused_rescue_methods_at_head_dim_256(method):
+    """The rescue methods on the Qwen3.5 shape: V1 routing, the d = 256 exact kernel, the rescue
+    choice (a thread pair per token, 128 dimensions each) and the fp32 rescue tail."""
+    shape = synthetic.LayerShape(1, 1409, 16, 4, 256)
+    q, k, v = synthetic.attention_inputs(shape, seed=47, needles=2, structured_sigma=0.5)
+    _fused_vs_oracle(method, q, k, v, 0.08, list(range(oracle.num_blocks(1409))))
+
+
+def test_rescue_tail_op_at_head_dim_256():
+    from exp3_b200 import kernels
+    shape = synthetic.LayerShape(1, 1153, 8, 2, 256)
+    q, k, v = synthetic.attention_inputs(shape, seed=48, needles=1)
+    g = torch.Generator().manual_seed(48)
+    selected = oracle.protected_selection(torch.rand(1, 10, 10, 8, generator=g), 0.6, 1, 1, 1)
+    for remainder in (False, True):
+        o, lse = kernels.rescue_tail(q.to(DEV), k.to(DEV), v.to(DEV), selected.to(DEV), SCALE, remainder=remainder)
+        o_ref, l_ref = oracle.rescue_tail(q.float(), k.float(), v.float(), selected, SCALE, remainder=remainder)
+        torch.testing.assert_close(lse.cpu(), l_ref, atol=LSE_TOL, rtol=0)
+        torch.testing.assert_close(o.cpu(), o_ref, atol=O_TOL, rtol=0)
 
 
 def test_decode_at_head_dim_256_matches_dense_softmax():
