@@ -79,3 +79,24 @@ def test_backend_configure_matches_reference_errors():
         backend.configure("flash")
     with pytest.raises(ValueError):
         ops.prefill_attention(None, None, None, "flash", 0.08, 1.0)
+
+
+def test_options_and_head_dims_on_the_host():
+    """fpx_set_option takes exactly the documented values; workspace sizes exist for head dims
+    128 and 256 and for nothing else (no GPU needed)."""
+    lib = _capi.lib()
+    for key, values in ((1, (0, 1, 2)), (2, (0, 2, 3)), (3, (0, 1)), (4, (0, 1)), (5, (0, 1))):
+        for value in values:
+            assert lib.fpx_set_option(key, value) == 0, (key, value)
+        assert lib.fpx_set_option(key, 7) == -1
+    for key, value in ((1, 0), (2, 0), (3, 0), (4, 0), (5, 0)):  # back to the defaults
+        assert lib.fpx_set_option(key, value) == 0
+    assert lib.fpx_set_option(6, 0) == -1 and lib.fpx_set_option(0, 0) == -1
+    for d, ok in ((128, True), (256, True), (64, False), (192, False)):
+        assert (lib.fpx_prefill_workspace_bytes(2, 1, 4096, 16, 4, d, 128) > 0) == ok, d
+        assert (lib.fpx_decode_workspace_bytes(1, 1, 16, 4, 4096, d) > 0) == ok, d
+        assert (lib.fpx_rescue_tail_workspace_bytes(1, 4096, 16, 4, d, 128) > 0) == ok, d
+    # the d = 256 workspace holds twice the descriptor bytes
+    assert lib.fpx_prefill_workspace_bytes(2, 1, 4096, 16, 4, 256, 128) > lib.fpx_prefill_workspace_bytes(
+        2, 1, 4096, 16, 4, 128, 128)
+    assert lib.fpx_ar_buffer_bytes(28672) == 768 + 2 * 8 * 28672 * 2 and lib.fpx_ar_buffer_bytes(12) == 0
