@@ -33,8 +33,23 @@ import torch
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
-# Keep rank 0's stdout to the one JSON line (NCCL otherwise announces its version there).
 os.environ.setdefault("NCCL_DEBUG", "WARN")
+
+# Rank 0's stdout carries exactly one JSON line. Libraries print to file descriptor 1 on their
+# own (NCCL announces its version there), so main() points descriptor 1 at stderr and the JSON
+# line is written to a saved duplicate of the real stdout.
+_JSON_OUT = None
+
+
+def quiet_stdout():
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.dup(1)
+    os.dup2(2, 1)
+
+
+def emit(line: dict):
+    os.write(_JSON_OUT if _JSON_OUT is not None else 1, (json.dumps(line) + "\n").encode())
 
 SCALE = 128 ** -0.5
 # Layer workloads (--config): c2 is the headline; c4 / c5 are BASELINE.json's long-sequence and
@@ -283,7 +298,7 @@ def run_reference(args, rank, world):
                        "variant": args.variant},
             "cpu_baseline": {**values[0], "value": value},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_model(args, rank, world, local):
@@ -376,7 +391,7 @@ def run_model(args, rank, world, local):
                 "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": ids_host.numel() * 8,
                         "d2h_bytes_per_step": 8},
                 "clocks": clocks.summary()}
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         model.close_comm()
         dist.barrier()
@@ -385,6 +400,7 @@ def run_model(args, rank, world, local):
 
 def main():
     args = parse()
+    quiet_stdout()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", args.gpus))
     local = int(os.environ.get("LOCAL_RANK", 0))
@@ -589,7 +605,7 @@ def main():
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
