@@ -90,3 +90,15 @@ def test_synthetic_prompt_plants_repeated_spans():
     assert ids.shape == (4096,) and int(ids.max()) < 1000
     assert torch.equal(ids, synthetic_prompt(4096, vocab=1000, spans=8, span_len=16, seed=1))
 
+
+
+def test_vocab_sharded_lm_head_reassembles():
+    """Under tensor parallelism each rank holds vocab / N rows of the LM head; the shards,
+    concatenated in rank order (the all-gather's order), are the replicated head."""
+    from exp3_b200.model import Qwen2Model
+    full = Qwen2Model(TINY, device="cpu", seed=3)
+    assert not full.vocab_sharded
+    for world in (2, 4):
+        shards = [Qwen2Model(TINY, device="cpu", seed=3, tp_rank=r, tp_size=world) for r in range(world)]
+        assert all(m.vocab_sharded for m in shards)
+        assert torch.equal(torch.cat([m.lm_head for m in shards]), full.lm_head)
