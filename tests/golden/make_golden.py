@@ -19,7 +19,9 @@ What runs, all on the CPU in fp32:
   ``explicit_mean_reference``, ``selector_reference``);
 - for head dim 256 (the Qwen3.5 shape, 16 query heads over 4 KV heads), the same Triton
   kernels with ``D_HEAD=256`` and the restatements in ``check_qwen35_math.py``
-  (``mean_reference``, ``score_reference``, ``selection_reference``, ``dense_reference``).
+  (``mean_reference``, ``score_reference``, ``selection_reference``, ``dense_reference``),
+  and the torch functions of ``kernels.py`` (descriptors, mean tail, selectors, rescue tails)
+  on d = 256 inputs.
 
 The interpreter cannot run bf16 (it yields NaN), so bf16 inputs are upcast to
 fp32 first; values stay bf16-representable. Inputs are not stored: they are
@@ -251,8 +253,35 @@ def main(root="/root/reference"):
         selected_fixed=selected.numpy(), indices_fixed=f_idx.numpy(), counts_fixed=f_cnt.numpy(),
         lse_fixed=lse_fixed.numpy(), out_fixed_rows=out_fixed[:, ::8][:, :, keep_heads].numpy(),
     )
+
+    # Case 6: head dim 256 for the mean-corrected methods and the rescue tails, L=1153 (10 blocks,
+    # the last with one row), 8 query heads over 2 KV heads: the reference's descriptors, mean
+    # tail and merge, its three selectors with their protected selection, and both rescue tails.
+    seed, length, heads, kv_heads = 49, 1153, 8, 2
+    q, k, v = inputs(seed, length, heads, kv_heads, 256)
+    q32, k32, v32 = q.float(), k.float(), v.float()
+    blocks = 10
+    desc = kernels.block_descriptors(k32, v32)
+    g = torch.Generator().manual_seed(seed)
+    selected = kernels.protected_selection(torch.rand(1, blocks, blocks, heads, generator=g), 0.6, 1, 1, 1)
+    m_out, m_lse = kernels.mean_tail(q32, desc, selected, scale256)
+    record = {"seed": seed, "length": length, "heads": heads, "kv_heads": kv_heads, "head_dim": 256,
+              "digest": synthetic.tensor_digest(q, k, v), "selected": selected.numpy(), "rows": np.arange(0, length, 9),
+              "out_heads": np.array([0, 3, 6]),
+              "desc_mean_k": desc.mean_k.numpy(), "desc_var_k": desc.var_k.numpy(),
+              "desc_mean_v": desc.mean_v.numpy(), "desc_sigma_v": desc.sigma_v.numpy(),
+              "mean_lse": m_lse.numpy(), "mean_out_rows": m_out[:, ::9][:, :, [0, 3, 6]].numpy()}
+    for selector in ("mean_balanced", "cgf_mean", "dispersion_mean"):
+        sc = kernels.selector_scores(q32, desc, scale256, selector, chunk_tiles=2)
+        record[f"{selector}_scores"] = sc.numpy()
+        record[f"{selector}_selected"] = kernels.protected_selection(sc, 0.08, 2, 4, 2).numpy()
+    for name, remainder in (("rescue", False), ("rescue_v2", True)):
+        o, lse = kernels.rescue_tail(q32, k32, v32, selected, scale256, chunk_tiles=3, remainder=remainder)
+        record[f"{name}_out_rows"] = o[:, ::9][:, :, [0, 3, 6]].numpy()
+        record[f"{name}_lse"] = lse.numpy()
+    np.savez_compressed(HERE / "qwen35_tails_l1153.npz", **record)
     for name in ("v1_routing_l1089.npz", "exact_mean_l257.npz", "selectors_l385.npz", "rescue_l1153.npz",
-                 "qwen35_routing_l1025.npz", "qwen35_exact_l385.npz"):
+                 "qwen35_routing_l1025.npz", "qwen35_exact_l385.npz", "qwen35_tails_l1153.npz"):
         print(name, (HERE / name).stat().st_size, "bytes")
 
 

@@ -150,3 +150,28 @@ def test_head_dim_256_exact_path_matches_reference():
     out, lse = oracle.exact_attention(q32, k32, v32, idx, cnt, 256 ** -0.5)
     torch.testing.assert_close(lse, t(data["lse_all"]), atol=2e-6, rtol=1e-5)
     torch.testing.assert_close(out[:, rows][:, :, heads], t(data["out_all_rows"]), atol=2e-6, rtol=1e-5)
+
+
+def test_head_dim_256_tails_and_selectors_match_reference():
+    """The oracle's descriptors, block-mean tail, selectors + selection and rescue tails at
+    d = 256 against the reference's own kernels.py functions on the same inputs."""
+    data, q, k, v = load("qwen35_tails_l1153.npz")
+    scale = 256 ** -0.5
+    q32, k32, v32 = q.float(), k.float(), v.float()
+    rows, heads = t(data["rows"]), t(data["out_heads"])
+    desc = oracle.block_descriptors(k32, v32)
+    for name in ("mean_k", "mean_v", "var_k", "sigma_v"):
+        torch.testing.assert_close(getattr(desc, name), t(data[f"desc_{name}"]), atol=1e-6, rtol=1e-5)
+    selected = t(data["selected"])
+    out, lse = oracle.mean_tail(q32, desc, selected, scale)
+    torch.testing.assert_close(lse, t(data["mean_lse"]), atol=2e-6, rtol=1e-5)
+    torch.testing.assert_close(out[:, rows][:, :, heads], t(data["mean_out_rows"]), atol=2e-6, rtol=1e-5)
+    for selector in oracle.SELECTORS:
+        scores = oracle.selector_scores(q32, desc, scale, selector)
+        torch.testing.assert_close(scores, t(data[f"{selector}_scores"]), atol=2e-5, rtol=2e-5)
+        sel = oracle.protected_selection(t(data[f"{selector}_scores"]), 0.08, 2, 4, 2)
+        assert torch.equal(sel, t(data[f"{selector}_selected"]))
+    for name, remainder in (("rescue", False), ("rescue_v2", True)):
+        o, l = oracle.rescue_tail(q32, k32, v32, selected, scale, remainder=remainder)
+        torch.testing.assert_close(l, t(data[f"{name}_lse"]), atol=2e-6, rtol=1e-5)
+        torch.testing.assert_close(o[:, rows][:, :, heads], t(data[f"{name}_out_rows"]), atol=2e-6, rtol=1e-5)
