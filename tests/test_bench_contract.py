@@ -41,3 +41,38 @@ def test_reference_arm_non_zero_ranks_print_nothing():
 def test_fewer_than_three_warmups_are_refused():
     res = run_bench("--impl", "reference", "--steps", "1", "--warmup", "1")
     assert res.returncode != 0
+
+
+def _bench_module():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_under_test", ROOT / "bench.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_sharding_covers_every_work_unit_once():
+    """bench.py's partition: for the layer configs at 1, 2, 4 and 8 ranks, the (KV group, tile
+    range) shards cover every (group, tile) exactly once, and the exact-pair counts of the
+    shards add up to the layer's (the oracle's accounting formula)."""
+    import torch
+
+    import oracle
+    bench = _bench_module()
+    g = torch.Generator().manual_seed(3)
+    for kv_heads, group, blocks, length in ((4, 7, 256, 32768), (8, 5, 64, 8193), (4, 4, 17, 2177)):
+        selected = torch.rand(1, blocks, blocks, kv_heads * group, generator=g) < 0.6
+        selected &= torch.tril(torch.ones(blocks, blocks, dtype=torch.bool)).view(1, blocks, blocks, 1)
+        total = bench.exact_pairs(selected, length, (0, kv_heads), (0, blocks), group)
+        assert total == oracle.exact_token_pairs(selected, length)
+        for world in (1, 2, 4, 8):
+            if world > kv_heads and world % kv_heads:
+                continue
+            seen = torch.zeros(kv_heads, blocks, dtype=torch.int32)
+            pairs = 0
+            for rank in range(world):
+                kv_range, tile_range = bench.partition(rank, world, kv_heads, blocks)
+                seen[kv_range[0]:kv_range[1], tile_range[0]:tile_range[1]] += 1
+                pairs += bench.exact_pairs(selected, length, kv_range, tile_range, group)
+            assert bool((seen == 1).all()), (kv_heads, blocks, world)
+            assert pairs == total
