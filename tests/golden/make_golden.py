@@ -280,8 +280,42 @@ def main(root="/root/reference"):
         record[f"{name}_out_rows"] = o[:, ::9][:, :, [0, 3, 6]].numpy()
         record[f"{name}_lse"] = lse.numpy()
     np.savez_compressed(HERE / "qwen35_tails_l1153.npz", **record)
+
+    # Case 7: edge lengths, L = 1 (one block of one row) and L = 129 (two blocks, the last with one
+    # row), 4 query heads over 2 KV heads: V1 block mean, scores and selection, the exact path over
+    # every causal block, and the mean tail and merge of a selection with one unselected block.
+    record = {}
+    for length in (1, 129):
+        seed = 60 + length
+        q, k, v = inputs(seed, length, 4, 2)
+        q32, k32, v32 = q.float(), k.float(), v.float()
+        blocks = (length + 127) // 128
+        mean32 = ref_block_mean(upstream, k32)
+        mk = mean32.to(torch.bfloat16)
+        scores = ref_v1_scores(upstream, q32, mk.float())
+        idx, cnt = deal(upstream, scores, 0.08)
+        every = kernels.protected_selection(torch.zeros(1, blocks, blocks, 4), 0.0, 2, 4, 2)
+        a_idx, a_cnt = kernels.indices_from_mask(every)
+        out_all, lse_all = ref_exact(upstream, q32, k32, v32, a_idx, a_cnt)
+        selected = every.clone()
+        if blocks > 1:
+            selected[:, 1, 0, ::2] = False  # heads 0 and 2 of the last tile lose block 0
+        desc = kernels.block_descriptors(k32, v32)
+        f_idx, f_cnt = kernels.indices_from_mask(selected)
+        out_f, lse_f = ref_exact(upstream, q32, k32, v32, f_idx, f_cnt)
+        m_out, m_lse = kernels.mean_tail(q32, desc, selected, SCALE)
+        merged, merged_lse = kernels.merge_exact_mean(out_f, lse_f, m_out, m_lse)
+        tag = f"l{length}"
+        record.update({f"{tag}_seed": seed, f"{tag}_digest": synthetic.tensor_digest(q, k, v),
+                       f"{tag}_block_mean_fp32": mean32.numpy(), f"{tag}_scores": scores.numpy(),
+                       f"{tag}_indices_a008": idx.numpy(), f"{tag}_counts_a008": cnt.numpy(),
+                       f"{tag}_out_all": out_all.numpy(), f"{tag}_lse_all": lse_all.numpy(),
+                       f"{tag}_selected": selected.numpy(), f"{tag}_merged": merged.numpy(),
+                       f"{tag}_merged_lse": merged_lse.numpy()})
+    np.savez_compressed(HERE / "edges_l1_l129.npz", **record)
     for name in ("v1_routing_l1089.npz", "exact_mean_l257.npz", "selectors_l385.npz", "rescue_l1153.npz",
-                 "qwen35_routing_l1025.npz", "qwen35_exact_l385.npz", "qwen35_tails_l1153.npz"):
+                 "qwen35_routing_l1025.npz", "qwen35_exact_l385.npz", "qwen35_tails_l1153.npz",
+                 "edges_l1_l129.npz"):
         print(name, (HERE / name).stat().st_size, "bytes")
 
 

@@ -175,3 +175,38 @@ def test_head_dim_256_tails_and_selectors_match_reference():
         o, l = oracle.rescue_tail(q32, k32, v32, selected, scale, remainder=remainder)
         torch.testing.assert_close(l, t(data[f"{name}_lse"]), atol=2e-6, rtol=1e-5)
         torch.testing.assert_close(o[:, rows][:, :, heads], t(data[f"{name}_out_rows"]), atol=2e-6, rtol=1e-5)
+
+
+def test_edge_lengths_match_reference():
+    """L = 1 and L = 129 (a one-row block): the oracle's V1 block mean, scores, selection, exact
+    path, mean tail and merge against the reference run on the same inputs."""
+    from exp3_b200 import synthetic
+    from golden_cases import GOLDEN
+    data = dict(np.load(GOLDEN / "edges_l1_l129.npz", allow_pickle=False))
+    for length in (1, 129):
+        tag = f"l{length}"
+        shape = synthetic.LayerShape(1, length, 4, 2)
+        q, k, v = synthetic.attention_inputs(shape, seed=int(data[f"{tag}_seed"]), needles=2, apply_rope=True)
+        assert synthetic.tensor_digest(q, k, v) == str(data[f"{tag}_digest"])
+        q32, k32, v32 = q.float(), k.float(), v.float()
+        mk = oracle.block_mean_k(k)
+        torch.testing.assert_close(mk.float(), t(data[f"{tag}_block_mean_fp32"]), atol=2e-3, rtol=2e-2)
+        ref_mk = t(data[f"{tag}_block_mean_fp32"]).to(torch.bfloat16)
+        scores = oracle.v1_scores(q, ref_mk, SCALE)
+        torch.testing.assert_close(scores, t(data[f"{tag}_scores"]), atol=1e-6, rtol=1e-5)
+        idx, cnt = oracle.deal_output_score(t(data[f"{tag}_scores"]), 2, 4, 0.08, 2, 0)
+        assert torch.equal(idx, t(data[f"{tag}_indices_a008"])) and torch.equal(cnt, t(data[f"{tag}_counts_a008"]))
+        blocks = (length + 127) // 128
+        every = oracle.protected_selection(torch.zeros(1, blocks, blocks, 4), 0.0, 2, 4, 2)
+        a_idx, a_cnt = oracle.indices_from_mask(every)
+        out, lse = oracle.exact_attention(q32, k32, v32, a_idx, a_cnt, SCALE)
+        torch.testing.assert_close(out, t(data[f"{tag}_out_all"]), atol=2e-6, rtol=1e-5)
+        torch.testing.assert_close(lse, t(data[f"{tag}_lse_all"]), atol=2e-6, rtol=1e-5)
+        selected = t(data[f"{tag}_selected"])
+        f_idx, f_cnt = oracle.indices_from_mask(selected)
+        eo, el = oracle.exact_attention(q32, k32, v32, f_idx, f_cnt, SCALE)
+        desc = oracle.block_descriptors(k32, v32)
+        mo, ml = oracle.mean_tail(q32, desc, selected, SCALE)
+        merged, merged_lse = oracle.merge_exact_mean(eo, el, mo, ml)
+        torch.testing.assert_close(merged.float(), t(data[f"{tag}_merged"]), atol=2e-6, rtol=1e-5)
+        torch.testing.assert_close(merged_lse, t(data[f"{tag}_merged_lse"]), atol=2e-6, rtol=1e-5)
