@@ -362,9 +362,12 @@ extern "C" int fpx_decode_attention_at(const void *q, int64_t q_sb, int64_t q_sl
 //
 // The first call on a device looks up the array's device address with cudaGetSymbolAddress (the
 // array's name in host code is only a host-side stand-in, not a device address); make that
-// first call before any stream capture. Every call shares the one array and it keeps the last
-// call's contents: each call writes every partial it later reads, so nothing has to start at
-// zero, but calls that overlap on the GPU (different streams, no ordering) race on the array.
+// first call before any stream capture. The address is cached per device index for the life of
+// the process, so the library must not be used across a cudaDeviceReset (or any other teardown
+// of the device's primary context): the cached address would then be stale. Every call shares
+// the one array and it keeps the last call's contents: each call writes every partial it later
+// reads, so nothing has to start at zero, but calls that overlap on the GPU (different streams,
+// no ordering) race on the array.
 namespace fpx {
 
 constexpr size_t kDecodeScratchBytes = FPX_DECODE_NOALLOC_SCRATCH_BYTES;
@@ -397,33 +400,12 @@ extern "C" int fpx_decode_attention_noalloc(const void *q, int64_t q_sb, int64_t
                                             void *out, int64_t o_sb, int64_t o_sl, int64_t o_sh,
                                             float *lse, fpx_stream_t stream) {
   FPX_BIND(stream);
-  if (d != kHeadDim && d != 256) return FPX_ERR_UNSUPPORTED;
-  if (!q || !k || !v || !out || B <= 0 || Lq <= 0 || S <= 0 || H <= 0 || Hkv <= 0)
-    return FPX_ERR_INVALID;
-  // Q, K and V rows move in 16-byte pieces: last dim contiguous, other strides multiples of 8.
-  if (H % Hkv || H / Hkv > kMaxGroup || k_sl % 8 || k_sb % 8 || k_sh % 8 || v_sl % 8 || v_sb % 8 ||
-      v_sh % 8 || q_sl % 8 || q_sb % 8 || q_sh % 8 || (reinterpret_cast<uintptr_t>(k) & 15) ||
-      (reinterpret_cast<uintptr_t>(v) & 15) || (reinterpret_cast<uintptr_t>(q) & 15))
-    return FPX_ERR_SHAPE;
-  // Sizes whose partials do not fit the fixed array are refused before anything runs.
+  // Sizes whose partials do not fit the fixed array are refused before anything runs. Invalid
+  // arguments size to 0 here and are refused by decode_run's own checks.
   if (fpx_decode_workspace_bytes(B, Lq, H, Hkv, S, d) > kDecodeScratchBytes) return FPX_ERR_WORKSPACE;
   void *scratch = nullptr;
   const int rc = decode_scratch_address(&scratch);
   if (rc != FPX_OK) return rc;
-  DecodeParams p{};
-  p.q = static_cast<const __nv_bfloat16 *>(q);
-  p.k = static_cast<const __nv_bfloat16 *>(k);
-  p.v = static_cast<const __nv_bfloat16 *>(v);
-  p.q_sb = q_sb; p.q_sl = q_sl; p.q_sh = q_sh;
-  p.k_sb = k_sb; p.k_sl = k_sl; p.k_sh = k_sh;
-  p.v_sb = v_sb; p.v_sl = v_sl; p.v_sh = v_sh;
-  p.out = static_cast<__nv_bfloat16 *>(out); p.o_sb = o_sb; p.o_sl = o_sl; p.o_sh = o_sh;
-  p.lse = lse; p.Lq = Lq; p.S = S; p.H = H; p.Hkv = Hkv; p.group = H / Hkv;
-  p.splits = decode_splits(B, Lq, Hkv, S);
-  p.keys_per_split = (((S + p.splits - 1) / p.splits) + kDecodeKeys - 1) / kDecodeKeys * kDecodeKeys;
-  p.splits = (S + p.keys_per_split - 1) / p.keys_per_split;
-  p.scale_log2 = (float)scale * kLog2e;
-  p.part_o = static_cast<float *>(scratch);
-  p.part_ml = p.part_o + (size_t)B * Lq * H * p.splits * d;
-  return decode_launch(p, d, B, Hkv, stream);
+  return decode_run(q, q_sb, q_sl, q_sh, k, k_sb, k_sl, k_sh, v, v_sb, v_sl, v_sh, B, Lq, S, nullptr, H, Hkv, d,
+                    scale, out, o_sb, o_sl, o_sh, lse, scratch, kDecodeScratchBytes, stream);
 }

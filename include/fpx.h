@@ -13,8 +13,8 @@
  * block scores [B, nb, nb, H] fp32 (query block, key block, head); block index
  * lists [B, nb, nb, H] int64 ascending with sentinel nb; counts [B, nb, H] int32;
  * masks [B, nb, nb, H] uint8 (0/1, torch.bool storage). nb = ceil(L / block).
- * Only block = 128 and d = 128 are compiled; other values return
- * FPX_ERR_UNSUPPORTED.
+ * Only block = 128 and head dim d in {128, 256} are compiled; other values
+ * return FPX_ERR_UNSUPPORTED.
  *
  * Reference file:line citations are to the exp3 tree; "upstream" means
  * upstream/flashprefill_native_forward.py.
@@ -281,8 +281,10 @@ int fpx_decode_attention_at(const void *q, int64_t q_sb, int64_t q_sl, int64_t q
  * it until the process exits. Problems whose partials
  * (fpx_decode_workspace_bytes(B, Lq, H, Hkv, S, d)) exceed that size return
  * FPX_ERR_WORKSPACE before anything runs. The first call on a device looks the array's
- * address up (cudaGetSymbolAddress), so make it before any stream capture. All calls share
- * the array: calls that overlap on the GPU race; nothing in it needs to start at zero. */
+ * address up (cudaGetSymbolAddress), so make it before any stream capture; the address is
+ * kept for the life of the process, so do not use the library across a cudaDeviceReset. All
+ * calls share the array: calls that overlap on the GPU race; nothing in it needs to start at
+ * zero. */
 #define FPX_DECODE_NOALLOC_SCRATCH_BYTES (2u << 20)
 int fpx_decode_attention_noalloc(const void *q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
                                  const void *k, int64_t k_sb, int64_t k_sl, int64_t k_sh,

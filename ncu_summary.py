@@ -1,6 +1,6 @@
 """Summarises an ncu CSV launch list (``--metrics gpu__time_duration.sum --csv``) per kernel.
 
-    python -m exp3_b200.ncu_summary launches.csv [--top 12]
+    python ncu_summary.py launches.csv [--top 12]
 
 Prints launches, total device time and share per kernel name. ncu serialises launches
 and runs them cold, so compare shares, not absolute times, with a bench run.

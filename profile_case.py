@@ -1,7 +1,7 @@
 """Runs the fused prefill attention layer a few times on one shape: the command profiled by ncu.
 
-    python -m exp3_b200.profile_case [--length 32768] [--head-dim 128|256] [--method mean_native] [--alpha 0.08]
-                                     [--repeats 3] [--variant iid|structured] [--kernel tcgen05]
+    python profile_case.py [--length 32768] [--head-dim 128|256] [--method mean_native] [--alpha 0.08]
+                           [--repeats 3] [--variant iid|structured] [--kernel tcgen05|tcgen05_single|mma]
 
 Exits 0 after printing per-stage CUDA-event times of the last repeat; it is meant to be run
 once plainly and then under ``ncu -k regex:<kernel> -s <skip> -c <count>``.
@@ -10,11 +10,15 @@ once plainly and then under ``ncu -k regex:<kernel> -s <skip> -c <count>``.
 from __future__ import annotations
 
 import argparse
+import sys
+from pathlib import Path
 
 import torch
 
-from . import _capi, ops, synthetic
-from ._capi import STAGE_EXACT, STAGE_MEAN, STAGE_ROUTE
+sys.path.insert(0, str(Path(__file__).resolve().parent))
+
+from exp3_b200 import _capi, ops, synthetic  # noqa: E402
+from exp3_b200._capi import STAGE_EXACT, STAGE_MEAN, STAGE_ROUTE  # noqa: E402
 
 
 def main():
@@ -27,7 +31,7 @@ def main():
     ap.add_argument("--alpha", type=float, default=0.08)
     ap.add_argument("--repeats", type=int, default=3)
     ap.add_argument("--variant", default="iid", choices=["iid", "structured"])
-    ap.add_argument("--kernel", default="tcgen05", choices=["tcgen05", "mma"])
+    ap.add_argument("--kernel", default="tcgen05", choices=["tcgen05", "tcgen05_single", "mma"])
     ap.add_argument("--emulate", type=int, default=0, choices=[0, 2, 3])
     args = ap.parse_args()
     dev = torch.device("cuda", 0)

@@ -76,3 +76,31 @@ def test_sharding_covers_every_work_unit_once():
                 pairs += bench.exact_pairs(selected, length, kv_range, tile_range, group)
             assert bool((seen == 1).all()), (kv_heads, blocks, world)
             assert pairs == total
+
+
+def test_world_sizes_that_leave_work_unowned_are_refused():
+    """With 4 KV groups, 3, 5, 6 or 7 ranks would either leave a group unowned or index past
+    the last group; partition refuses them instead of reporting work nobody did."""
+    import pytest
+    bench = _bench_module()
+    for world in (3, 5, 6, 7):
+        with pytest.raises(ValueError):
+            bench.partition(0, world, 4, 256)
+
+
+def test_tile_cut_fills_whole_waves():
+    """Config 2 at 8 ranks (two ranks per KV group): the simulated CTA schedule of the chosen cut
+    finishes no later than the causal-work median cut (tile 181 of 256), whose late rank leaves a
+    near-empty third wave of long tiles."""
+    import torch
+    bench = _bench_module()
+    nb, group, heads = 256, 7, 28
+    selected = torch.tril(torch.ones(nb, nb, dtype=torch.bool)).view(1, nb, nb, 1).expand(1, nb, nb, heads)
+    costs = bench.cta_costs(selected.contiguous(), group)
+    (_, _), (c0, c1) = bench.partition(0, 8, 4, nb, costs=costs, sms=148)
+    assert c0 == 0
+    span = lambda cut: max(bench.makespan(costs, (0, 1), (0, cut), 148), bench.makespan(costs, (0, 1), (cut, nb), 148))
+    assert span(c1) <= span(181)
+    assert span(c1) < 0.95 * span(181)
+    # the two ranks of a group share its tiles exactly
+    assert bench.partition(1, 8, 4, nb, costs=costs, sms=148) == ((0, 1), (c1, nb))
