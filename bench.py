@@ -159,13 +159,13 @@ def cta_costs(selected, group, paired=True):
 
 def makespan(costs, kv_range, tile_range, sms):
     """List-schedules the exact kernel's grid on ``sms`` SMs, one CTA per SM, in launch order
-    (x: the tiles, longest first; y: KV group x head unit; z: batch) and returns when the last
-    CTA ends, in blocks."""
+    (x: KV group x head unit, fastest; y: the tiles, longest first; z: batch) and returns when
+    the last CTA ends, in blocks."""
     import heapq
     t0, t1 = tile_range
     if t1 <= t0:
         return 0.0
-    c = costs[:, kv_range[0]:kv_range[1], :, t0:t1].flip(-1).reshape(-1).tolist()
+    c = costs[:, kv_range[0]:kv_range[1], :, t0:t1].flip(-1).permute(0, 3, 1, 2).reshape(-1).tolist()
     free = [0.0] * sms
     for w in c:
         heapq.heappush(free, heapq.heappop(free) + w + CTA_OVERHEAD_BLOCKS)

@@ -107,9 +107,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem &sh = *reinterpret_cast<Smem *>(smem_raw + pad);
   volatile int *abort = &sh.abort;
 
-  const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);
-  const int pair = blockIdx.y % pairs;
-  const int kvh = p.head_begin / p.group + blockIdx.y / pairs;
+  // x: (KV group, head pair), fastest; y: tile, longest tail first; z: batch.
+  const int t = p.tile_begin + (gridDim.y - 1 - blockIdx.y);
+  const int pair = blockIdx.x % pairs;
+  const int kvh = p.head_begin / p.group + blockIdx.x / pairs;
   const int b = blockIdx.z;
   const int hA = kvh * p.group + 2 * pair;
   const bool has_b = 2 * pair + 1 < p.group;
@@ -422,7 +423,7 @@ int launch_mean_tail_tc(const MeanParams &p, int B, int tiles, int heads, cudaSt
       !encode_4d(&to, p.out, d, p.H, p.L, B, p.o_sh, p.o_sl, p.o_sb))
     return FPX_ERR_INVALID;
   const int pairs = (p.group + 1) / 2;
-  const dim3 grid(tiles, (heads / p.group) * pairs, B);
+  const dim3 grid((heads / p.group) * pairs, tiles, B);
   const size_t smem = mean_tail_tc_smem();
   cudaFuncSetAttribute(mean_tail_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   mean_tail_tc_kernel<<<grid, kThreads, smem, s>>>(tq, tmkh, tmkl, tmv, to, p, pairs, p.scale * kLog2e,

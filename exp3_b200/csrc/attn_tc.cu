@@ -103,9 +103,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem &sh = *reinterpret_cast<Smem *>(smem_raw + pad);
   volatile int *abort = &sh.abort;
 
-  const int t = p.tile_begin + (gridDim.x - 1 - blockIdx.x);  // longest tiles first
-  const int pair = blockIdx.y % pairs;
-  const int kvh = p.head_begin / p.group + blockIdx.y / pairs;
+  // x: (KV group, head pair), fastest; y: tile, longest first; z: batch. The hardware starts
+  // CTAs in x-fastest order, so the whole grid runs longest tile first, and the head pairs of a
+  // KV group read the same K/V blocks at about the same time.
+  const int t = p.tile_begin + (gridDim.y - 1 - blockIdx.y);
+  const int pair = blockIdx.x % pairs;
+  const int kvh = p.head_begin / p.group + blockIdx.x / pairs;
   const int b = blockIdx.z;
   const int hA = kvh * p.group + 2 * pair;
   const bool has_b = 2 * pair + 1 < p.group;
@@ -477,7 +480,7 @@ int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int 
       !encode_4d(&to, p.out, kHeadDim, p.H, L, B, p.o_sh, p.o_sl, p.o_sb))
     return FPX_ERR_INVALID;
   const int pairs = (p.group + 1) / 2;
-  const dim3 grid(tiles, (heads / p.group) * pairs, B);
+  const dim3 grid((heads / p.group) * pairs, tiles, B);
   const size_t smem = exact_tc_smem();
   switch (get_option(kOptExpEmulation)) {
     case 0: launch_variant<0>(grid, smem, s, tq, tk, tv, to, p, pairs); break;

@@ -140,12 +140,14 @@ __global__ void __launch_bounds__(kThreads1, 1)
   Smem1<D> &sh = *reinterpret_cast<Smem1<D> *>(smem_raw + pad);
   volatile int *abort = &sh.abort;
 
+  // x: (KV group, head), fastest, so a group's heads are adjacent and read the same K/V blocks
+  // at about the same time; y: tile, longest first over the whole grid; z: batch.
   const int G = p.group;
-  const int kv_local = blockIdx.z % p.kv_count;
-  const int b = blockIdx.z / p.kv_count;
+  const int kv_local = blockIdx.x / G;
+  const int b = blockIdx.z;
   const int kvh = p.head_begin / G + kv_local;
-  const int head = kvh * G + blockIdx.x;
-  const int t = p.tile_begin + (gridDim.y - 1 - blockIdx.y);  // longest tiles first
+  const int head = kvh * G + blockIdx.x % G;
+  const int t = p.tile_begin + (gridDim.y - 1 - blockIdx.y);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool failed = err && *reinterpret_cast<volatile int *>(err) != 0;
 
@@ -440,7 +442,7 @@ int launch_exact_tc1(const ExactParams &p, int d, int B, int L, int Hkv, int til
     return FPX_ERR_INVALID;
   ExactParams q = p;
   q.kv_count = heads / p.group;
-  const dim3 grid(p.group, tiles, q.kv_count * B);
+  const dim3 grid(p.group * q.kv_count, tiles, B);
   int *err = device_error_word();
   if (d == 128)
     launch_d<128>(grid, s, tq, tk, tv, to, q, err);

@@ -21,6 +21,14 @@ Tensor parallelism (``tp_size`` > 1, one process per GPU, NCCL):
 - QKV and gate/up are column-sharded, o_proj and down_proj row-sharded;
 - o_proj and down_proj are each followed by an all-reduce.
 
+The tensor-parallel prefill overlaps those all-reduces with compute. Routing and attention
+of a query tile read only that tile's rows and the K/V rows before it, and every other op is
+row-wise, so each layer runs as ``prefill_chunks`` row chunks (whole 128-row tiles): chunk c
+goes through RMSNorm, QKV, RoPE, attention on its tile range and o_proj, and its o_proj
+all-reduce is issued asynchronously while chunk c + 1 computes; the MLP of chunk c runs after
+that, and its down all-reduce overlaps the following chunks (and the next layer's first ones).
+Only the last chunk's o_proj all-reduce of each layer is left exposed.
+
 The embedding and LM head are replicated; only the last token's logits are computed.
 """
 
@@ -177,6 +185,8 @@ class Qwen2Model:
         self.length = 0
         self.peer_all_reduce = True
         self._peer_ar = None
+        # Row chunks of the tensor-parallel prefill pipeline (1 = one pass per layer, no overlap).
+        self.prefill_chunks = 4 if tp_size > 1 else 1
         self.replay_events = None  # (start, end, replays) of the last decode_graph
 
     # ---------------------------------------------------------------- pieces
@@ -279,18 +289,103 @@ class Qwen2Model:
             return full
         return logits[-1]
 
+    def _chunk_bounds(self, length: int):
+        """Row ranges [r0, r1) of the prefill pipeline: ``prefill_chunks`` runs of whole tiles."""
+        tiles = (length + 127) // 128
+        n = max(1, min(self.prefill_chunks, tiles))
+        cuts = [round(tiles * c / n) for c in range(n + 1)]
+        return [(128 * a, min(length, 128 * b)) for a, b in zip(cuts, cuts[1:]) if b > a]
+
+    def _forward_pipelined(self, ids):
+        """The tensor-parallel prefill as a row-chunk pipeline (see the module docstring): the
+        same computation as ``_forward(ids, 0, decoding=False)``, with each chunk's all-reduces
+        issued asynchronously and waited for only by the compute that reads them."""
+        cfg = self.cfg
+        d, hid = cfg.head_dim, cfg.hidden_size
+        hq, hkv = len(self.qh), len(self.kv)
+        length = ids.shape[0]
+        bounds = self._chunk_bounds(length)
+        dev = self.device
+        h = torch.nn.functional.embedding(ids, self.embed)
+        x = torch.empty_like(h)
+        o = torch.empty_like(h)
+        down = torch.empty_like(h)
+        qkv = torch.empty(length, (hq + 2 * hkv) * d, dtype=torch.bfloat16, device=dev)
+        attn = torch.empty(length, hq * d, dtype=torch.bfloat16, device=dev)
+        q = qkv[:, : hq * d].view(1, length, hq, d)
+        k = qkv[:, hq * d:(hq + hkv) * d].view(1, length, hkv, d)
+        v = qkv[:, (hq + hkv) * d:].view(1, length, hkv, d)
+        a = self.attn
+        pending_down = [None] * len(bounds)  # down all-reduce of chunk c, previous layer
+        work_o = [None] * len(bounds)
+
+        def attention_part(i, c):
+            lw = self.layers[i]
+            r0, r1 = bounds[c]
+            if pending_down[c] is not None:
+                pending_down[c].wait()
+                pending_down[c] = None
+            if i == 0:
+                x[r0:r1] = self._rmsnorm(h[r0:r1], lw.ln1)
+            else:
+                x[r0:r1] = self._rmsnorm(down[r0:r1], lw.ln1, residual=h[r0:r1])  # h += down
+            torch.addmm(lw.b_qkv, x[r0:r1], lw.w_qkv.t(), out=qkv[r0:r1])
+            self._rope(q[:, r0:r1], r0)
+            self._rope(k[:, r0:r1], r0)
+            self.k_cache[i, :, r0:r1] = k[:, r0:r1]
+            self.v_cache[i, :, r0:r1] = v[:, r0:r1]
+            ops.prefill_attention(q, k, v, a.method, a.alpha, self.scale, a.sink, a.window, a.last_full,
+                                  out=attn.view(1, length, hq, d), tile_range=(r0 // 128, (r1 + 127) // 128))
+            torch.mm(attn[r0:r1], lw.w_o.t(), out=o[r0:r1])
+            work_o[c] = torch.distributed.all_reduce(o[r0:r1], group=self.group, async_op=True)
+
+        def mlp_part(i, c):
+            lw = self.layers[i]
+            r0, r1 = bounds[c]
+            work_o[c].wait()
+            work_o[c] = None
+            x2 = self._rmsnorm(o[r0:r1], lw.ln2, residual=h[r0:r1])  # h += o
+            torch.mm(self._silu_mul(x2 @ lw.w_gu.t()), lw.w_down.t(), out=down[r0:r1])
+            pending_down[c] = torch.distributed.all_reduce(down[r0:r1], group=self.group, async_op=True)
+
+        for i in range(cfg.num_hidden_layers):
+            for c in range(len(bounds)):
+                attention_part(i, c)
+                if c > 0:
+                    mlp_part(i, c - 1)
+            mlp_part(i, len(bounds) - 1)
+        for c, work in enumerate(pending_down):
+            if work is not None:
+                work.wait()
+        last = self._rmsnorm(down[-1:].contiguous(), self.norm, residual=h[-1:].contiguous())
+        logits = (last @ self.lm_head.t()).float()
+        if self.vocab_sharded:
+            full = torch.empty(self.tp_size * logits.shape[-1], dtype=logits.dtype, device=logits.device)
+            torch.distributed.all_gather_into_tensor(full, logits.view(-1), group=self.group)
+            return full
+        return logits[-1]
+
     # ---------------------------------------------------------------- public
     @torch.inference_mode()
-    def prefill(self, input_ids: torch.Tensor, max_new_tokens: int = 0):
-        """``evaluate.prefill``: one forward over the prompt; returns the first generated token (device)."""
+    def prefill_logits(self, input_ids: torch.Tensor, max_new_tokens: int = 0):
+        """One forward over the prompt (filling the KV cache); returns the last token's fp32
+        logits over the whole vocabulary, on the device."""
         if input_ids.dim() != 1:
             raise ValueError("input_ids must be 1-D (batch 1, as exp3)")
         length = input_ids.shape[0]
         if self.k_cache is None or self.k_cache.shape[2] < length + max_new_tokens:
             self._alloc_cache(length + max_new_tokens)
-        logits = self._forward(input_ids, 0, decoding=False)
+        if self.tp_size > 1 and self.prefill_chunks > 1:
+            logits = self._forward_pipelined(input_ids)
+        else:
+            logits = self._forward(input_ids, 0, decoding=False)
         self.length = length
-        return logits.argmax()
+        return logits
+
+    @torch.inference_mode()
+    def prefill(self, input_ids: torch.Tensor, max_new_tokens: int = 0):
+        """``evaluate.prefill``: one forward over the prompt; returns the first generated token (device)."""
+        return self.prefill_logits(input_ids, max_new_tokens).argmax()
 
     @torch.inference_mode()
     def decode_step(self, token: torch.Tensor):

@@ -4,7 +4,8 @@ Same names, arguments, return types and layouts ([batch, sequence, heads, dim]) 
 the reference module (``upstream:420-533``); every op allocates fresh outputs and
 never mutates its inputs. The Triton kernels and ``torch.compile`` helpers of the
 reference are replaced by the CUDA kernels of libfpx (routing: csrc/route.cu;
-exact path: csrc/attn_*.cu).
+exact path: csrc/attn_*.cu). Each op is also the PyTorch custom op
+``torch.ops.fpx.<name>`` (with a fake implementation), which the public functions call.
 """
 
 from __future__ import annotations
@@ -33,9 +34,8 @@ def _check_bf16(*tensors):
             raise TypeError(f"expected bfloat16 tensors, got {t.dtype}")
 
 
-@torch.no_grad()
-def block_mean_k(k: torch.Tensor, block_size: int = 128) -> torch.Tensor:
-    """``upstream:420-442``: bf16 mean of each (block, KV head) -> [B, nb, Hkv, d]."""
+@torch.library.custom_op("fpx::block_mean_k", mutates_args=())
+def _block_mean_k(k: torch.Tensor, block_size: int) -> torch.Tensor:
     dev = require_cuda(k)
     _check_bf16(k)
     batch, sequence, kv_heads, head_dim = k.shape
@@ -45,9 +45,20 @@ def block_mean_k(k: torch.Tensor, block_size: int = 128) -> torch.Tensor:
     return mean
 
 
+@_block_mean_k.register_fake
+def _(k, block_size):
+    batch, sequence, kv_heads, head_dim = k.shape
+    return k.new_empty(batch, _blocks(sequence, block_size), kv_heads, head_dim)
+
+
 @torch.no_grad()
-def v1_scores(q: torch.Tensor, mean_k: torch.Tensor, scale: float, block_size: int = 128) -> torch.Tensor:
-    """``upstream:445-475``: normalised V1 proxy scores [B, nb, nb, H] fp32."""
+def block_mean_k(k: torch.Tensor, block_size: int = 128) -> torch.Tensor:
+    """``upstream:420-442``: bf16 mean of each (block, KV head) -> [B, nb, Hkv, d]."""
+    return torch.ops.fpx.block_mean_k(k, block_size)
+
+
+@torch.library.custom_op("fpx::v1_scores", mutates_args=())
+def _v1_scores(q: torch.Tensor, mean_k: torch.Tensor, scale: float, block_size: int) -> torch.Tensor:
     dev = require_cuda(q, mean_k)
     _check_bf16(q, mean_k)
     batch, sequence, heads, head_dim = q.shape
@@ -59,10 +70,21 @@ def v1_scores(q: torch.Tensor, mean_k: torch.Tensor, scale: float, block_size: i
     return score
 
 
+@_v1_scores.register_fake
+def _(q, mean_k, scale, block_size):
+    blocks = mean_k.shape[1]
+    return q.new_empty(q.shape[0], blocks, blocks, q.shape[2], dtype=torch.float32)
+
+
 @torch.no_grad()
-def deal_output_score(score: torch.Tensor, attention_sink: int, window: int, alpha: float = 0.1,
-                      last_n_blocks_full: int = 2, min_budget: int = 0):
-    """``upstream:388-407``: (int64 indices [B, nb, nb, H] with sentinel nb, int32 counts [B, nb, H])."""
+def v1_scores(q: torch.Tensor, mean_k: torch.Tensor, scale: float, block_size: int = 128) -> torch.Tensor:
+    """``upstream:445-475``: normalised V1 proxy scores [B, nb, nb, H] fp32."""
+    return torch.ops.fpx.v1_scores(q, mean_k, float(scale), block_size)
+
+
+@torch.library.custom_op("fpx::deal_output_score", mutates_args=())
+def _deal_output_score(score: torch.Tensor, attention_sink: int, window: int, alpha: float,
+                       last_n_blocks_full: int, min_budget: int) -> tuple[torch.Tensor, torch.Tensor]:
     dev = require_cuda(score)
     score = score.float().contiguous()
     batch, query_blocks, key_blocks, heads = score.shape
@@ -75,9 +97,24 @@ def deal_output_score(score: torch.Tensor, attention_sink: int, window: int, alp
     return indices, counts
 
 
+@_deal_output_score.register_fake
+def _(score, attention_sink, window, alpha, last_n_blocks_full, min_budget):
+    batch, query_blocks, _, heads = score.shape
+    return (score.new_empty(score.shape, dtype=torch.int64),
+            score.new_empty(batch, query_blocks, heads, dtype=torch.int32))
+
+
 @torch.no_grad()
-def exact_attention(q, k, v, indices, counts, scale: float, block_size: int = 128):
-    """``upstream:478-521``: (bf16 output [B, L, H, d], fp32 natural LSE [B, L, H])."""
+def deal_output_score(score: torch.Tensor, attention_sink: int, window: int, alpha: float = 0.1,
+                      last_n_blocks_full: int = 2, min_budget: int = 0):
+    """``upstream:388-407``: (int64 indices [B, nb, nb, H] with sentinel nb, int32 counts [B, nb, H])."""
+    return torch.ops.fpx.deal_output_score(score, attention_sink, window, float(alpha), last_n_blocks_full,
+                                           min_budget)
+
+
+@torch.library.custom_op("fpx::exact_attention", mutates_args=())
+def _exact_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                     counts: torch.Tensor, scale: float, block_size: int) -> tuple[torch.Tensor, torch.Tensor]:
     dev = require_cuda(q, k, v, indices, counts)
     _check_bf16(q, k, v)
     batch, sequence, heads, head_dim = q.shape
@@ -89,6 +126,17 @@ def exact_attention(q, k, v, indices, counts, scale: float, block_size: int = 12
          ptr(indices), ptr(counts), batch, sequence, heads, k.shape[2], head_dim, block_size, float(scale),
          ptr(output), ptr(lse), stream(dev))
     return output, lse
+
+
+@_exact_attention.register_fake
+def _(q, k, v, indices, counts, scale, block_size):
+    return torch.empty_like(q, memory_format=torch.contiguous_format), q.new_empty(q.shape[:3], dtype=torch.float32)
+
+
+@torch.no_grad()
+def exact_attention(q, k, v, indices, counts, scale: float, block_size: int = 128):
+    """``upstream:478-521``: (bf16 output [B, L, H, d], fp32 natural LSE [B, L, H])."""
+    return torch.ops.fpx.exact_attention(q, k, v, indices, counts, float(scale), block_size)
 
 
 def attention_tile_sizes():

@@ -107,28 +107,26 @@ def _tp_rank(rank, world, port, q):
         ids = torch.randint(0, cfg.vocab_size, (1500,), generator=torch.Generator().manual_seed(12)).to(dev)
         settings = AttentionSettings("mean_native", 0.08)
         single = Qwen2Model(cfg, device=dev, seed=13, attention=settings)
-        split = Qwen2Model(cfg, device=dev, seed=13, tp_rank=rank, tp_size=world, attention=settings)
-        assert split.qh == ([0, 1] if rank == 0 else [2])
         checks = []
-        with torch.inference_mode():
-            single.prefill(ids, max_new_tokens=8)
-            split.prefill(ids, max_new_tokens=8)
-            ref = single._forward(ids, 0, decoding=False)
-            got = split._forward(ids, 0, decoding=False)
-            for step in range(5):
-                ok, (err, _, _) = _close(got, ref)
-                checks.append(ok and _same_token(got, ref, err))
-                if step == 4:
-                    break
-                token = ref.argmax().view(1)  # teacher-forced: both models decode the TP = 1 token
-                ref = single._forward(token, single.length, decoding=True)
-                single.length += 1
-                got = split._forward(token, split.length, decoding=True)
-                split.length += 1
-        if split._peer_ar is not None:
-            dist.barrier()
-            split._peer_ar.close()
-        result = checks if not all(checks) else True
+        # TP = 2 as one pass per layer, and as the 4-chunk pipeline with overlapped all-reduces
+        for chunks in (1, 4):
+            split = Qwen2Model(cfg, device=dev, seed=13, tp_rank=rank, tp_size=world, attention=settings)
+            split.prefill_chunks = chunks
+            assert split.qh == ([0, 1] if rank == 0 else [2])
+            with torch.inference_mode():
+                ref = single.prefill_logits(ids, max_new_tokens=8)
+                got = split.prefill_logits(ids, max_new_tokens=8)
+                for step in range(5):
+                    ok, (err, _, _) = _close(got, ref)
+                    checks.append((chunks, step, ok and _same_token(got, ref, err), err))
+                    if step == 4:
+                        break
+                    token = ref.argmax().view(1)  # teacher-forced: both models decode the TP = 1 token
+                    ref = single._forward(token, single.length, decoding=True)
+                    single.length += 1
+                    got = split._forward(token, split.length, decoding=True)
+                    split.length += 1
+        result = True if all(c[2] for c in checks) else checks
     except Exception as exc:  # reported to the parent, which fails the test
         result = repr(exc)
     finally:
