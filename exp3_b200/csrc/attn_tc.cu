@@ -244,24 +244,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else if (warp == 9) {
-      // ------------------------------------------------------------ MMA issuer
-      if (n_union > 0 && mbar_wait_warp(&sh.q_full, 0, abort)) {
+      // ------------------------------------------------------------ MMA issuer (lane 0 alone)
+      // The issuing thread bounds the kernel (one product per ~100 cycles), so it runs alone,
+      // without warp votes, and waits for the K and V stages before it waits for P: a stage
+      // has landed long before P is written, so those waits stay off the softmax -> P.V ->
+      // QK^T chain.
+      if (lane == 0 && n_union > 0 && mbar_wait(&sh.q_full, 0, abort)) {
         int pend[2] = {-1, -1}, n_pv[2] = {0, 0};
         // P.V of tile x for its pending block; frees the V stage once no tile still needs it.
         auto flush = [&](int x) -> bool {
           const int u = pend[x], s = u % kVStages;
-          if (!mbar_wait_warp(&sh.p_full[x], n_pv[x] & 1, abort)) return false;
-          if (!mbar_wait_warp(&sh.v_full[s], (u / kVStages) & 1, abort)) return false;
+          if (!mbar_wait(&sh.v_full[s], (u / kVStages) & 1, abort)) return false;
+          if (!mbar_wait(&sh.p_full[x], n_pv[x] & 1, abort)) return false;
           tc_fence_after();
-          if (lane == 0) {
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              mma_ts(tmem + 256 + 128 * x, tmem + 128 * x + 8 * kk, desc_v(sh.v[s], kk), kIdescPV,
-                     (n_pv[x] > 0 || kk > 0) ? 1u : 0u);
-            tc_commit(&sh.o_done[x]);
-            if (pend[x ^ 1] != u) tc_commit(&sh.v_empty[s]);
-          }
-          __syncwarp();
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ts(tmem + 256 + 128 * x, tmem + 128 * x + 8 * kk, desc_v(sh.v[s], kk), kIdescPV,
+                   (n_pv[x] > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&sh.o_done[x]);
+          if (pend[x ^ 1] != u) tc_commit(&sh.v_empty[s]);
           ++n_pv[x];
           pend[x] = -1;
           return true;
@@ -272,38 +273,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           // The V producer refills this block's V stage only after block u - kVStages's P.V.
           for (int x = 0; x < 2 && ok; ++x)
             if (u >= kVStages && pend[x] == u - kVStages) ok = flush(x);
+          if (!ok || !(ok = mbar_wait(&sh.k_full[s], (u / kKStages) & 1, abort))) break;
           const int flags = sh.u_flags[u];
-          bool have_k = false;
           for (int x = 0; x < 2 && ok; ++x) {
             if (!(flags & (1 << x))) continue;
             if (pend[x] >= 0 && !(ok = flush(x))) break;
-            if (!have_k && !(ok = mbar_wait_warp(&sh.k_full[s], (u / kKStages) & 1, abort))) break;
-            have_k = true;
             tc_fence_after();
-            if (lane == 0) {
 #pragma unroll
-              for (int kk = 0; kk < 8; ++kk)
-                mma_ss(tmem + 128 * x, desc_kmajor(sh.q[x], kk), desc_kmajor(sh.k[s], kk), kIdescQK,
-                       kk > 0 ? 1u : 0u);
-              tc_commit(&sh.s_full[x]);
-            }
-            __syncwarp();
+            for (int kk = 0; kk < 8; ++kk)
+              mma_ss(tmem + 128 * x, desc_kmajor(sh.q[x], kk), desc_kmajor(sh.k[s], kk), kIdescQK,
+                     kk > 0 ? 1u : 0u);
+            tc_commit(&sh.s_full[x]);
             pend[x] = u;
           }
-          if (ok && have_k) {  // both tiles' QK^T of block u issued: its K stage can be refilled
-            if (lane == 0) tc_commit(&sh.k_empty[s]);
-            __syncwarp();
-          }
+          if (ok) tc_commit(&sh.k_empty[s]);  // both tiles' QK^T of block u issued: refill its K stage
         }
         for (int x = 0; x < 2 && ok && !*abort; ++x)
           if (pend[x] >= 0) ok = flush(x);
         if (*abort) {  // let every MMA this thread issued finish before TMEM is released
           int never = 0;
-          if (lane == 0) tc_commit(&sh.drain);
-          __syncwarp();
+          tc_commit(&sh.drain);
           mbar_wait(&sh.drain, 0, &never);
         }
       }
+      __syncwarp();
     }
   } else {
     regs_inc<kSoftmaxRegs>();
@@ -342,9 +335,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 8; ++c) mx[c] = sv[c];
 #pragma unroll
-      for (int c = 8; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
-      const float bmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
+      for (int c = 8; c < 128; c += 16)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx[j] = fmax3(mx[j], sv[c + j], sv[c + 8 + j]);
+      const float bmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7])) * sl2;
       const float mn = fmaxf(m, bmax);
       float corr = 1.f;
       // Each row decides for itself (rows never influence one another's rounding); rows that

@@ -132,6 +132,12 @@ FPX_INLINE void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32
       : "memory");
 }
 // 2^x on the special-function unit (the hardware's approximate exp2, flush-to-zero).
+// Maximum of three floats in one instruction (the three-input max.f32 of sm_100).
+FPX_INLINE float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 FPX_INLINE float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
