@@ -438,6 +438,16 @@ def model_measure(args, rank, world, local, dev, steps):
     for _ in range(args.warmup):
         model.prefill(ids, args.decode_tokens)
     torch.cuda.synchronize()
+    # Tensor parallel: the prefill runs as one pass per layer or as the 4-chunk pipeline that
+    # overlaps its all-reduces (Qwen2Model._forward_pipelined); both are timed after the warm-up
+    # (max over ranks, so every rank makes the same choice) and the faster one is used and reported.
+    by_chunks = {}
+    if world > 1:
+        for chunks in (1, 4):
+            model.prefill_chunks = chunks
+            model.prefill(ids, args.decode_tokens)
+            by_chunks[chunks] = _timed(lambda: model.prefill(ids, args.decode_tokens), 2, world, dev)
+        model.prefill_chunks = min(by_chunks, key=by_chunks.get)
     with clocks:
         prefill_ms = _timed(lambda: model.prefill(ids, args.decode_tokens), steps, world, dev)
     first = model.prefill(ids, args.decode_tokens)
@@ -467,11 +477,13 @@ def model_measure(args, rank, world, local, dev, steps):
 
     e2e_ms = _timed(e2e, steps, world, dev)
     flops = model.prefill_flops(args.prompt_length)  # linear + all causal attention pairs
+    model_chunks = model.prefill_chunks
     if world > 1:
         model.close_comm()
     del model
     torch.cuda.empty_cache()
-    return {"prefill_ms": prefill_ms, "e2e_ms": e2e_ms, "tp": world,
+    return {"prefill_ms": prefill_ms, "e2e_ms": e2e_ms, "tp": world, "prefill_chunks": model_chunks,
+            "prefill_ms_by_chunks": by_chunks or None,
             "prefill_tflops_dense_equivalent": flops / (prefill_ms * 1e-3) / 1e12,
             "decode_ms_per_token": decode_ms, "decode_ms_per_token_eager": decode_eager_ms,
             "decode_replay_ms_per_token": replay_ms, "steps": steps,

@@ -102,3 +102,19 @@ def test_vocab_sharded_lm_head_reassembles():
         shards = [Qwen2Model(TINY, device="cpu", seed=3, tp_rank=r, tp_size=world) for r in range(world)]
         assert all(m.vocab_sharded for m in shards)
         assert torch.equal(torch.cat([m.lm_head for m in shards]), full.lm_head)
+
+
+@pytest.mark.parametrize("length,chunks", [(32640, 4), (1500, 4), (100, 4), (129, 8), (32640, 1)])
+def test_prefill_pipeline_chunks_are_whole_tiles_covering_every_row(length, chunks):
+    """The tensor-parallel prefill pipeline's row chunks: contiguous, in order, every boundary
+    on a 128-row tile (so each chunk's attention is a tile range), together every row once."""
+    from exp3_b200.model import Qwen2Model
+    model = Qwen2Model.__new__(Qwen2Model)  # host logic only: no weights
+    model.prefill_chunks = chunks
+    bounds = model._chunk_bounds(length)
+    tiles = (length + 127) // 128
+    assert 1 <= len(bounds) <= min(chunks, tiles)
+    assert bounds[0][0] == 0 and bounds[-1][1] == length
+    for (a0, a1), (b0, b1) in zip(bounds, bounds[1:]):
+        assert a1 == b0
+    assert all(r0 % 128 == 0 and r0 < r1 for r0, r1 in bounds)
