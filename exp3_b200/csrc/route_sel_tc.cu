@@ -9,12 +9,19 @@
 //   score = mean over the tile's rows of p (x sqrt(u) x sigma_v for dispersion_mean)
 //   keep  = score > 0 and score >= alpha * max score, plus the protected blocks.
 //
-// The products run on the tensor core in two passes over 128-block chunks:
+// The products run on the tensor core over 128-block chunks:
 //   pass 1, row layout (TMEM lane = query row): S = Q . mean_K^T (and Q^2 . var_K^T); each
 //     thread keeps its row's running max and sum, giving the row's log-sum-exp;
-//   pass 2, transposed (TMEM lane = block): S^T = mean_K . Q^T (and var_K . (Q^2)^T); each
-//     thread owns one block and adds up its rows' probabilities (row LSEs from shared memory),
-//     so the column sums need no cross-thread reduction.
+//   column sums of the probabilities, in one of two ways:
+//   - a tile with at most two chunks (t <= 256, every tile of a 32K layer): pass 1 writes each
+//     logit back into its accumulator column (and dispersion_mean's sqrt(u) weight into the u
+//     column); both chunks stay resident in the two TMEM buffers, and once the row LSEs are
+//     known each warp sums its 32 rows of every column with a 5-round shuffle butterfly
+//     (32 columns per 31 shuffles), the four warps meeting in shared memory. No product runs
+//     twice;
+//   - longer tiles: pass 2, transposed (TMEM lane = block): S^T = mean_K . Q^T (and
+//     var_K . (Q^2)^T); each thread owns one block and adds up its rows' probabilities (row
+//     LSEs from shared memory), so the column sums need no cross-thread reduction.
 // Precision: the fp32 descriptors enter as bf16 high + low halves (mean_k = hi + lo, lo the
 // rounding remainder), and Q^2 (exact in fp32: a bf16 square has 16 significant bits) splits
 // exactly into bf16 hi + lo; u accumulates Q2hi.VKhi + Q2lo.VKhi + Q2hi.VKlo. Logits carry about
@@ -59,6 +66,7 @@ struct alignas(1024) SelSmem {
   int abort;
   float lse[128];
   float part_m[2][128], part_s[2][128];  // the two warpgroups' halves
+  float colpart[2][4][64];              // resident path: [warpgroup][warp][column] partial sums
   float red[2][8];
   int scan[2][4 * (kMaxBlocks / 128)];
   float sc[kMaxBlocks];
@@ -102,7 +110,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kvh = h / p.group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int chunks = (t + 127) / 128;  // visible blocks kb < t
-  const int units = 2 * chunks;        // pass 1 then pass 2, chunk by chunk
+  // At most two chunks: their logits stay resident in the two TMEM buffers, no second pass.
+  const bool resident = chunks <= 2;
+  const int units = resident ? chunks : 2 * chunks;  // pass 1 (then pass 2), chunk by chunk
 
   if (threadIdx.x == 0) {
     mbar_init(&sh.q_full, 1);
@@ -269,8 +279,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           float cmax = -INFINITY;
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
-            vl[c] = c0 + c < ncol ? sel_logit<kSel>(vl[c], kSel > 0 ? vu[c] : 0.f, scale, scale2) * kLog2e : -INFINITY;
-            cmax = fmaxf(cmax, vl[c]);
+            const float x = c0 + c < ncol ? sel_logit<kSel>(vl[c], kSel > 0 ? vu[c] : 0.f, scale, scale2) * kLog2e
+                                          : -INFINITY;
+            if (kSel == 2) vu[c] = sqrtf(fmaxf(__fmul_rn(vu[c], scale2), 0.f));  // dispersion weight
+            vl[c] = x;
+            cmax = fmaxf(cmax, x);
+          }
+          if (resident) {  // keep the logits (and weights) for the column sums
+            tmem_st32(tmem + lane_off + kAccStride * a + c0, vl);
+            if (kSel == 2) tmem_st32(tmem + lane_off + kAccStride * a + 128 + c0, vu);
           }
           const float mn = fmaxf(m, cmax);
           if (mn != -INFINITY) {
@@ -285,8 +302,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&sh.acc_empty[a]);
+      if (resident) {
+        tmem_wait_st();
+      } else {
+        tc_fence_before();
+        mbar_arrive(&sh.acc_empty[a]);
+      }
     }
     sh.part_m[g][e] = m;
     sh.part_s[g][e] = ssum;
@@ -299,8 +320,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       sh.lse[e] = mm + __log2f(s0 + s1);
     }
     all_sync();
+    // Resident path: p = 2^(logit - LSE) from the kept logits; warp ew sums its 32 rows of each
+    // 32-column slice by a shuffle butterfly (after the rounds lane l holds column l), the
+    // four warps' partials meet in shared memory, and group 0 forms block kb = 128 c + e.
+    for (int c = 0; resident && c < chunks; ++c) {
+      const int ncol = min(128, t - 128 * c);
+      const float lse_row = sh.lse[e];
+      const bool row_ok = e < rows;
+#pragma unroll 1
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const int c0 = 64 * g + 32 * q2;
+        float v[32];
+        if (ok && c0 < ncol) {
+          float w[32];
+          tmem_ld32(tmem + lane_off + kAccStride * c + c0, v);
+          if (kSel == 2) tmem_ld32(tmem + lane_off + kAccStride * c + 128 + c0, w);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float x = (row_ok && c0 + i < ncol) ? ex2(v[i] - lse_row) : 0.f;
+            if (kSel == 2) x *= w[i];
+            v[i] = x;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+          const bool upper = (lane & o) != 0;
+#pragma unroll
+          for (int i = 0; i < o; ++i) {
+            const float send = upper ? v[i] : v[i + o];
+            const float keep = upper ? v[i + o] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+          }
+        }
+        sh.colpart[g][ew][32 * q2 + lane] = v[0];
+      }
+      all_sync();
+      if (g == 0 && 128 * c + e < p.nb) {
+        const int kb = 128 * c + e, gc = e >> 6, col = e & 63;
+        float score = 0.f;
+        if (kb < t) {
+          float total = (sh.colpart[gc][0][col] + sh.colpart[gc][1][col]) +
+                        (sh.colpart[gc][2][col] + sh.colpart[gc][3][col]);
+          if (kSel == 2) total *= p.sigma_v[((int64_t)b * p.nb + kb) * p.Hkv + kvh];
+          score = total / (float)rows;
+        }
+        sh.sc[kb] = score;
+      }
+      all_sync();
+    }
     // Pass 2: block kb = 128 c + e sums the probabilities of this group's rows.
-    for (int u = chunks; u < 2 * chunks; ++u) {
+    for (int u = chunks; !resident && u < 2 * chunks; ++u) {
       const int a = u & 1, c = u - chunks;
       if (ok) ok = mbar_wait_warp(&sh.acc_full[a], (u >> 1) & 1, abort);
       tc_fence_after();
