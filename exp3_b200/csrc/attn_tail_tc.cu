@@ -118,6 +118,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int words = p.route.words;
   const bool failed = *reinterpret_cast<volatile int *>(device_error) != 0;
+  if (failed) return;
+  // A tile has a tail iff some block kb < t went unselected: its selected count (blocks <= t,
+  // the diagonal always among them) is then below t + 1. A CTA whose tiles both have none
+  // leaves before it touches the bitmaps or a barrier: the exact output stands.
+  {
+    const int c_a = p.route.counts[p.route.row(b, hA, t, p.H)];
+    const int c_b = has_b ? p.route.counts[p.route.row(b, hA + 1, t, p.H)] : t + 1;
+    if (c_a >= t + 1 && c_b >= t + 1) return;
+  }
 
   // Tail bits of both tiles, then the chunks that hold any tail column (ascending, with flags).
   for (int x = 0; x < 2; ++x) {
@@ -220,23 +229,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (issued[s] > 0) mbar_wait(is_k ? &sh.k_full[s] : &sh.v_full[s], (issued[s] - 1) & 1, &never);
       }
     } else if (warp == 9) {
-      // ------------------------------------------------------------ MMA issuer
-      if (mbar_wait_warp(&sh.q_full, 0, abort)) {
+      // ------------------------------------------------------------ MMA issuer (lane 0 alone)
+      // One thread issues every product, without warp votes around its waits, and it waits for
+      // a chunk's mean-V stage before it waits for that chunk's P (the stage lands long before).
+      if (lane == 0 && mbar_wait(&sh.q_full, 0, abort)) {
         int pend[2] = {-1, -1}, n_pv[2] = {0, 0};
         auto flush = [&](int x) -> bool {  // P_x . V of tile x's pending chunk
           const int u = pend[x], s = u & 1;
-          if (!mbar_wait_warp(&sh.p_full[x], n_pv[x] & 1, abort)) return false;
-          if (!mbar_wait_warp(&sh.v_full[s], (u >> 1) & 1, abort)) return false;
+          if (!mbar_wait(&sh.v_full[s], (u >> 1) & 1, abort)) return false;
+          if (!mbar_wait(&sh.p_full[x], n_pv[x] & 1, abort)) return false;
           tc_fence_after();
-          if (lane == 0) {
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              mma_ts(tmem + 256 + 128 * x, tmem + 128 * x + 8 * kk, desc_v(sh.v[s], kk), kIdescPV,
-                     (n_pv[x] > 0 || kk > 0) ? 1u : 0u);
-            tc_commit(&sh.o_done[x]);
-            if (pend[x ^ 1] != u) tc_commit(&sh.v_empty[s]);
-          }
-          __syncwarp();
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ts(tmem + 256 + 128 * x, tmem + 128 * x + 8 * kk, desc_v(sh.v[s], kk), kIdescPV,
+                   (n_pv[x] > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&sh.o_done[x]);
+          if (pend[x ^ 1] != u) tc_commit(&sh.v_empty[s]);
           ++n_pv[x];
           pend[x] = -1;
           return true;
@@ -249,20 +257,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int x = 0; x < 2 && ok; ++x)
             if ((flags & (1 << x)) && pend[x] >= 0) ok = flush(x);
           for (int part = 0; part < 2 && ok; ++part) {
-            if (!(ok = mbar_wait_warp(&sh.k_full[part], u & 1, abort))) break;
+            if (!(ok = mbar_wait(&sh.k_full[part], u & 1, abort))) break;
             tc_fence_after();
-            if (lane == 0) {
-              for (int x = 0; x < 2; ++x) {
-                if (!(flags & (1 << x))) continue;
+            for (int x = 0; x < 2; ++x) {
+              if (!(flags & (1 << x))) continue;
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                  mma_ss(tmem + 128 * x, desc_kmajor(sh.q[x], kk), desc_kmajor(sh.k[part], kk), kIdescQK,
-                         (part > 0 || kk > 0) ? 1u : 0u);
-                if (part == 1) tc_commit(&sh.s_full[x]);
-              }
-              tc_commit(&sh.k_empty[part]);
+              for (int kk = 0; kk < 8; ++kk)
+                mma_ss(tmem + 128 * x, desc_kmajor(sh.q[x], kk), desc_kmajor(sh.k[part], kk), kIdescQK,
+                       (part > 0 || kk > 0) ? 1u : 0u);
+              if (part == 1) tc_commit(&sh.s_full[x]);
             }
-            __syncwarp();
+            tc_commit(&sh.k_empty[part]);
           }
           if (ok)
             for (int x = 0; x < 2; ++x)
@@ -272,11 +277,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (pend[x] >= 0) ok = flush(x);
         if (*abort) {
           int never = 0;
-          if (lane == 0) tc_commit(&sh.drain);
-          __syncwarp();
+          tc_commit(&sh.drain);
           mbar_wait(&sh.drain, 0, &never);
         }
       }
+      __syncwarp();
     }
   } else {
     regs_inc<kSoftmaxRegs>();
