@@ -267,9 +267,12 @@ size_t v1_route_smem(int nb, int d) {
 }
 
 int launch_v1_route_selected(const V1Params &p, int tiles, int heads, int B, cudaStream_t s) {
-  // The tcgen05 routing kernel is written for d = 128; head dim 256 takes the mma.sync one.
-  return (get_option(kOptRouteKernel) == kRouteKernelMmaSync || p.d == 256) ? launch_v1_route(p, tiles, heads, B, s)
-                                                                            : launch_v1_route_tc(p, B, tiles, heads, s);
+  // The tcgen05 routing kernel holds up to 2048 blocks at head dim 128 and 512 at 256 (its
+  // score arrays live in shared memory); longer head-dim-256 layers take the mma.sync kernel.
+  const int d = p.d == 256 ? 256 : kHeadDim;
+  return (get_option(kOptRouteKernel) == kRouteKernelMmaSync || !v1_route_tc_supports(d, p.nb))
+             ? launch_v1_route(p, tiles, heads, B, s)
+             : launch_v1_route_tc(p, B, tiles, heads, s);
 }
 
 int launch_v1_route(const V1Params &p, int tiles, int heads, int B, cudaStream_t s) {

@@ -64,6 +64,8 @@ int launch_block_stats(const StatsParams &p, int blocks, int kv_count, int B, bo
 int launch_v1_route(const V1Params &p, int tiles, int heads, int B, cudaStream_t s);
 // tcgen05 form (route_tc.cu): persistent CTAs over (b, KV group, tile) items.
 int launch_v1_route_tc(const V1Params &p, int B, int tiles, int heads, cudaStream_t s);
+// Whether the tcgen05 routing kernel holds a layer of nb blocks at head dim d.
+bool v1_route_tc_supports(int d, int nb);
 // The kernel fpx_set_option(3, ...) selects.
 int launch_v1_route_selected(const V1Params &p, int tiles, int heads, int B, cudaStream_t s);
 // tcgen05 form (route_sel_tc.cu): needs the bf16 splits in p (the fused path's workspace).

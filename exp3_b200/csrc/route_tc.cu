@@ -11,9 +11,10 @@
 // The product is computed transposed, D = mean_K . Q^T, so TMEM lane = key block and column =
 // query row: one thread owns one block and reduces its 128 query rows without any shuffle.
 // A persistent CTA walks work items (b, KV group, tile t), longest tiles first, and inside an
-// item the G heads of the group; each (head, 128-block chunk) is one unit of 8 MMAs
-// (M = 128 blocks, N = 128 rows, K = 128). 320 threads:
-//   warp 0       TMA: Q tiles (3-stage ring) and block-mean chunks
+// item the G heads of the group; each (head, 128-block chunk) is one unit of d / 16 MMAs
+// (M = 128 blocks, N = 128 rows, K = d; head dim 128 or 256). 320 threads:
+//   warp 0       TMA: Q tiles (3-stage ring at d = 128, one stage at d = 256, whose 64 KB
+//                tiles leave room for two resident block-mean chunks) and block-mean chunks
 //   warp 1       MMA issuer (one elected lane), TMEM owner
 //   warps 2..9   epilogue, two warpgroups taking alternate heads: thread = block (TMEM lane),
 //                then the head's normalisation and selection over the group's named barrier
@@ -36,17 +37,25 @@ namespace {
 using namespace tc;
 
 constexpr int kThreads = 320;
-constexpr int kQStages = 3;
 constexpr int kAcc = 4;                   // 128-column accumulators in 512 TMEM columns:
                                           // slots 2g, 2g + 1 belong to epilogue warpgroup g
-constexpr int kMaxBlocks = 2048;          // L <= 262144
-constexpr uint32_t kHalf = 128 * 128;     // 128 rows x 64 bf16, one SW128 half tile
-constexpr uint32_t kTile = 2 * kHalf;     // 128 x 128 bf16
+constexpr uint32_t kHalf = 128 * 128;     // 128 rows x 64 bf16, one SW128 atom
 constexpr uint32_t kIdesc = idesc_bf16(128, 128, false);
 
+// Per head dim: Q ring depth and the longest layer (blocks) the score arrays hold.
+template <int D>
+struct RouteGeo {
+  static constexpr int kAtoms = D / 64;                    // 64-column SW128 atoms per tile
+  static constexpr uint32_t kTile = kAtoms * kHalf;         // 128 x D bf16
+  static constexpr int kQStages = D == 128 ? 3 : 1;
+  static constexpr int kMaxBlocks = D == 128 ? 2048 : 512;  // L <= 262144 / 65536
+};
+
+template <int D>
 struct alignas(1024) Smem {
-  uint8_t q[kQStages][kTile];
-  uint8_t mk[2][kTile];
+  static constexpr int kQStages = RouteGeo<D>::kQStages, kMaxBlocks = RouteGeo<D>::kMaxBlocks;
+  uint8_t q[kQStages][RouteGeo<D>::kTile];
+  uint8_t mk[2][RouteGeo<D>::kTile];
   uint64_t q_full[kQStages], q_empty[kQStages], mk_full[2], mk_empty[2], acc_full[kAcc], acc_empty[kAcc];
   uint64_t drain;
   uint32_t tmem_base;
@@ -131,12 +140,15 @@ FPX_INLINE Item item_at(int i, int B, int tiles, int kv_groups, int kv_begin, in
 }  // namespace
 
 // Items run longest tile first; CTA c takes items c, c + gridDim.x, ...
+template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     v1_route_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_mk,
                        V1Params p, int B, int tiles, int kv_groups, int splits, int n_items, int *device_error) {
+  constexpr int kQStages = RouteGeo<D>::kQStages, kAtoms = RouteGeo<D>::kAtoms;
+  constexpr uint32_t kTile = RouteGeo<D>::kTile;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  Smem &sh = *reinterpret_cast<Smem *>(smem_raw + pad);
+  Smem<D> &sh = *reinterpret_cast<Smem<D> *>(smem_raw + pad);
   volatile int *abort = &sh.abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kv_begin = p.head_begin / p.group;
@@ -176,8 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (mk_use[slot] > 0 && !mbar_wait_warp(&sh.mk_empty[slot], (mk_use[slot] - 1) & 1, abort)) return false;
       if (lane == 0) {
         mbar_expect_tx(&sh.mk_full[slot], kTile);
-        tma_load_4d(sh.mk[slot], &tm_mk, &sh.mk_full[slot], 0, it.kvh, c * 128, it.b);
-        tma_load_4d(sh.mk[slot] + kHalf, &tm_mk, &sh.mk_full[slot], 64, it.kvh, c * 128, it.b);
+        for (int at = 0; at < kAtoms; ++at)
+          tma_load_4d(sh.mk[slot] + at * kHalf, &tm_mk, &sh.mk_full[slot], 64 * at, it.kvh, c * 128, it.b);
       }
       ++mk_use[slot];
       return true;
@@ -190,8 +202,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           const int h = it.kvh * G + hi;
           mbar_expect_tx(&sh.q_full[s], kTile);
-          tma_load_4d(sh.q[s], &tm_q, &sh.q_full[s], 0, h, it.t * 128, it.b);
-          tma_load_4d(sh.q[s] + kHalf, &tm_q, &sh.q_full[s], 64, h, it.t * 128, it.b);
+          for (int at = 0; at < kAtoms; ++at)
+            tma_load_4d(sh.q[s] + at * kHalf, &tm_q, &sh.q_full[s], 64 * at, h, it.t * 128, it.b);
         }
         ++q_n;
         if (it.resident) {
@@ -233,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           if (lane == 0) {
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
+            for (int kk = 0; kk < D / 16; ++kk)
               mma_ss(tmem + 128 * a, desc_kmajor(sh.mk[slot], kk), desc_kmajor(sh.q[s], kk), kIdesc,
                      kk > 0 ? 1u : 0u);
             tc_commit(&sh.acc_full[a]);
@@ -396,19 +408,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-size_t v1_route_tc_smem() { return sizeof(Smem) + 1024; }
+template <int D>
+size_t v1_route_tc_smem() { return sizeof(Smem<D>) + 1024; }
 
-int launch_v1_route_tc(const V1Params &p, int B, int tiles, int heads, cudaStream_t s) {
+template <int D>
+static int launch_v1_route_tc_d(const V1Params &p, int B, int tiles, int heads, cudaStream_t s) {
   if (tiles <= 0 || heads <= 0) return FPX_OK;
   if (heads % p.group || p.head_begin % p.group) return FPX_ERR_SHAPE;
-  if (p.nb > kMaxBlocks) return FPX_ERR_UNSUPPORTED;
+  if (p.nb > RouteGeo<D>::kMaxBlocks) return FPX_ERR_UNSUPPORTED;
   const int kv_groups = heads / p.group;
   // Split each group's heads over more items when the launch has fewer than two items per SM
   // (a tile range of one rank, a short sequence): an item's heads run one after another.
   CUtensorMap tq, tmk;
-  if (!encode_4d(&tq, p.q, kHeadDim, p.H, p.L, B, p.q_sh, p.q_sl, p.q_sb) ||
-      !encode_4d(&tmk, p.mean_k, kHeadDim, p.Hkv, p.nb, B, kHeadDim, (int64_t)p.Hkv * kHeadDim,
-                 (int64_t)p.nb * p.Hkv * kHeadDim))
+  if (!encode_4d(&tq, p.q, D, p.H, p.L, B, p.q_sh, p.q_sl, p.q_sb) ||
+      !encode_4d(&tmk, p.mean_k, D, p.Hkv, p.nb, B, D, (int64_t)p.Hkv * D, (int64_t)p.nb * p.Hkv * D))
     return FPX_ERR_INVALID;
   int *device_error = device_error_word();
   if (!device_error) return FPX_ERR_CUDA;
@@ -420,11 +433,20 @@ int launch_v1_route_tc(const V1Params &p, int B, int tiles, int heads, cudaStrea
   const int splits = std::max(1, std::min(p.group, (2 * sms + base_items - 1) / base_items));
   const int n_items = base_items * splits;
   const int grid = std::min(n_items, sms);
-  const size_t smem = v1_route_tc_smem();
-  cudaFuncSetAttribute(v1_route_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  v1_route_tc_kernel<<<grid, kThreads, smem, s>>>(tq, tmk, p, B, tiles, kv_groups, splits, n_items, device_error);
+  const size_t smem = v1_route_tc_smem<D>();
+  cudaFuncSetAttribute(v1_route_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  v1_route_tc_kernel<D><<<grid, kThreads, smem, s>>>(tq, tmk, p, B, tiles, kv_groups, splits, n_items, device_error);
   FPX_CHECK_LAUNCH();
   return FPX_OK;
+}
+
+int launch_v1_route_tc(const V1Params &p, int B, int tiles, int heads, cudaStream_t s) {
+  return p.d == 256 ? launch_v1_route_tc_d<256>(p, B, tiles, heads, s)
+                    : launch_v1_route_tc_d<128>(p, B, tiles, heads, s);
+}
+
+bool v1_route_tc_supports(int d, int nb) {
+  return d == 256 ? nb <= RouteGeo<256>::kMaxBlocks : nb <= RouteGeo<128>::kMaxBlocks;
 }
 
 }  // namespace fpx

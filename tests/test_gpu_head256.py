@@ -207,3 +207,30 @@ def test_decode_at_head_dim_256_matches_dense_softmax():
         w = torch.einsum("bqhd,bkhd->bhqk", q.float(), kf).mul(SCALE).softmax(-1)
         ref = torch.einsum("bhqk,bkhd->bqhd", w, vf)
         torch.testing.assert_close(out, ref, atol=O_TOL, rtol=0)
+
+
+@pytest.mark.parametrize("length,heads,kv", [(2049, 16, 4), (32768, 16, 4), (40000, 8, 4), (65536, 4, 2)])
+def test_tcgen05_and_mma_route_kernels_agree_at_head_dim_256(length, heads, kv):
+    """The tensor-core V1 routing at d = 256 (16 K-steps per chunk, one 64 KB Q stage, two
+    resident block-mean chunks) against the mma.sync kernel: scores within fp32 rounding, masks
+    bit-exact outside the threshold band. 40000 tokens give 313 blocks, so tiles past 256
+    blocks stream their block means; 65536 tokens give 512 blocks, the most the kernel holds at
+    d = 256."""
+    from test_gpu_parity import assert_masks_match
+    shape = synthetic.LayerShape(1, length, heads, kv, 256)
+    q, k, v = (x.to(DEV) for x in synthetic.attention_inputs(shape, seed=length + 256, needles=3,
+                                                              structured_sigma=0.5))
+    mk = upstream.block_mean_k(k)
+    scores, sels = [], []
+    try:
+        for which in ("mma", "tcgen05"):
+            _capi.set_route_kernel(which)
+            scores.append(upstream.v1_scores(q, mk, SCALE).cpu())
+            ops.prefill_attention(q, k, v, "fp_v1", 0.08, SCALE)
+            sels.append(ops.export_routing("fp_v1", 1, length, heads, kv, head_dim=256)[0].cpu())
+    finally:
+        _capi.set_route_kernel("tcgen05")
+    torch.testing.assert_close(scores[1], scores[0], atol=1e-6, rtol=1e-5)
+    blocks = oracle.num_blocks(length)
+    assert_masks_match("fp_v1", sels[1], sels[0], scores[0], 0.08, list(range(blocks)))
+    assert _capi.device_error() == 0
