@@ -25,6 +25,8 @@
 // error word; roles drain their copies and MMAs and exit.
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "attn.cuh"
 #include "tc.cuh"
 
@@ -420,11 +422,16 @@ int launch_mean_tail_tc(const MeanParams &p, int B, int tiles, int heads, cudaSt
   int *device_error = device_error_word();
   if (!device_error) return FPX_ERR_CUDA;
   const int64_t d = kHeadDim, dstride = (int64_t)p.Hkv * kHeadDim, bstride = (int64_t)p.nb * dstride;
+  // The block means exist only for the blocks before the launch's last tile (a shard computes
+  // no more), and a chunk of 128 blocks reaches past them: the maps end there, so the copy
+  // fills those rows with zeros instead of reading stale workspace (whose NaNs would survive
+  // the masked columns' P = 0 in P.V).
+  const int64_t mean_blocks = std::min<int64_t>(p.nb, (int64_t)p.tile_begin + tiles);
   CUtensorMap tq, tmkh, tmkl, tmv, to;
   if (!encode_4d(&tq, p.q, d, p.H, p.L, B, p.q_sh, p.q_sl, p.q_sb) ||
-      !encode_4d(&tmkh, p.mk_hi, d, p.Hkv, p.nb, B, kHeadDim, dstride, bstride) ||
-      !encode_4d(&tmkl, p.mk_lo, d, p.Hkv, p.nb, B, kHeadDim, dstride, bstride) ||
-      !encode_4d(&tmv, p.mv_hi, d, p.Hkv, p.nb, B, kHeadDim, dstride, bstride) ||
+      !encode_4d(&tmkh, p.mk_hi, d, p.Hkv, mean_blocks, B, kHeadDim, dstride, bstride) ||
+      !encode_4d(&tmkl, p.mk_lo, d, p.Hkv, mean_blocks, B, kHeadDim, dstride, bstride) ||
+      !encode_4d(&tmv, p.mv_hi, d, p.Hkv, mean_blocks, B, kHeadDim, dstride, bstride) ||
       !encode_4d(&to, p.out, d, p.H, p.L, B, p.o_sh, p.o_sl, p.o_sb))
     return FPX_ERR_INVALID;
   const int pairs = (p.group + 1) / 2;

@@ -4,7 +4,8 @@
     rank's (KV group range, query-tile range) of ``bench.partition`` writes disjoint rows and
     heads; together, for N = 2, 4 and 8, the shards reassemble the unsharded output and LSE
     bit for bit. One GPU runs every shard in turn (the shards share nothing, so this is the
-    same computation each rank does).
+    same computation each rank does). So do ranges cut at odd tiles. Each shard's workspace
+    starts as NaN bytes, as a rank's fresh workspace may hold anything.
 (b) The tensor-parallel model (``exp3_b200.model``, ``evaluate.py:324-345`` for what is timed):
     TP = 2 against TP = 1 on the same seed, with one KV head over two ranks and a 3-head group
     split 2 + 1 (the split-group path that Qwen2.5-7B takes at 8 GPUs as 4 + 3). Last-token
@@ -37,7 +38,7 @@ def _bench():
     return mod
 
 
-@pytest.mark.parametrize("method", ["mean_native", "cgf_mean"])
+@pytest.mark.parametrize("method", ["mean_native", "cgf_mean", "fp_v1_rescue"])
 def test_layer_shards_reassemble_the_unsharded_output(method):
     bench = _bench()
     dev = torch.device("cuda", 0)
@@ -46,7 +47,8 @@ def test_layer_shards_reassemble_the_unsharded_output(method):
     shape = synthetic.LayerShape(1, length, heads, kv_heads)
     q, k, v = synthetic.attention_inputs(shape, seed=21, needles=8, device=dev, structured_sigma=0.5)
     lse_full = torch.empty(1, length, heads, device=dev)
-    ws = torch.empty(ops.workspace_bytes(method, 1, length, heads, kv_heads, d), dtype=torch.uint8, device=dev)
+    # Every workspace starts as NaN bytes: no stage may read what it did not write in the same call.
+    ws = torch.full((ops.workspace_bytes(method, 1, length, heads, kv_heads, d),), 0xFF, dtype=torch.uint8, device=dev)
     full = ops.prefill_attention(q, k, v, method, 0.08, scale, lse=lse_full, ws=ws)
     selected, _, _ = ops.export_routing(method, 1, length, heads, kv_heads, ws=ws, device=dev)
     density = float(selected.sum()) / (heads * blocks * (blocks + 1) / 2)
@@ -58,12 +60,24 @@ def test_layer_shards_reassemble_the_unsharded_output(method):
         lse = torch.full_like(lse_full, float("nan"))
         for rank in range(world):
             kv_range, tile_range = bench.partition(rank, world, kv_heads, blocks, costs=costs, sms=sms)
-            shard_ws = torch.empty_like(ws)
+            shard_ws = torch.full_like(ws, 0xFF)
             ops.prefill_attention(q, k, v, method, 0.08, scale, out=out, lse=lse, ws=shard_ws,
                                   kv_range=kv_range, tile_range=tile_range)
         torch.cuda.synchronize()
-        assert torch.equal(out.view(torch.int16), full.view(torch.int16)), world
-        assert torch.equal(lse, lse_full), world
+        assert torch.equal(out.view(torch.int16), full.view(torch.int16)), (world, _differs(out, full, lse, lse_full))
+        assert torch.equal(lse, lse_full), (world, _differs(out, full, lse, lse_full))
+    # Ranges of odd length, of one tile, and starting at an odd tile: the exact kernel pairs the
+    # odd head's tiles from the top of each range, so each split pairs different tiles; a tile's
+    # result does not depend on the tile it shares a CTA with.
+    out = torch.full_like(full, float("nan"))
+    lse = torch.full_like(lse_full, float("nan"))
+    for tile_range in ((0, 37), (37, 38), (38, 41), (41, blocks)):
+        shard_ws = torch.full_like(ws, 0xFF)
+        ops.prefill_attention(q, k, v, method, 0.08, scale, out=out, lse=lse, ws=shard_ws,
+                              kv_range=(0, kv_heads), tile_range=tile_range)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), full.view(torch.int16)), _differs(out, full, lse, lse_full)
+    assert torch.equal(lse, lse_full), _differs(out, full, lse, lse_full)
     # the routing of one shard alone equals the unsharded routing on its tiles and heads
     kv_range, tile_range = bench.partition(1, 8, kv_heads, blocks, costs=costs, sms=sms)
     shard_ws = torch.zeros_like(ws)
@@ -73,6 +87,12 @@ def test_layer_shards_reassemble_the_unsharded_output(method):
     h0, h1 = kv_range[0] * group, kv_range[1] * group
     t0, t1 = tile_range
     assert torch.equal(sel_shard[:, t0:t1, :, h0:h1], selected[:, t0:t1, :, h0:h1])
+
+
+def _differs(out, full, lse, lse_full):
+    """Where a reassembled output differs from the unsharded one: (rows, query tiles, heads)."""
+    rows = ((out.view(torch.int16) != full.view(torch.int16)).any(-1) | (lse != lse_full)).nonzero()
+    return rows.shape[0], sorted({int(t) for t in rows[:, 1] // 128}), sorted({int(h) for h in rows[:, 2]})
 
 
 def _close(a, b, rel=3e-2):
