@@ -36,6 +36,7 @@ import subprocess
 import sys
 import threading
 import time
+import typing
 from pathlib import Path
 
 import torch
@@ -131,43 +132,81 @@ def inputs(variant, device, config="c2"):
     return synthetic.config_inputs(config, seed=0, device=device, **kw)
 
 
-# A CTA of the two-tile exact kernel that holds one head (the odd head of a 7-head group) runs
-# its block chain without a second tile to overlap, at about this fraction of a pair's time.
-SINGLE_HEAD_CTA_WEIGHT = 0.65
+# A CTA of the two-tile exact kernel that holds one tile alone (the last tile of a shard's range
+# for the odd head of a group, the pairing of that head running tiles t and t - 1 together) runs
+# the same per-block chain as a pair: measured at about this fraction of a pair's time.
+LONE_TILE_CTA_WEIGHT = 0.94
 # Per-CTA set-up and epilogue (TMEM allocation, block-list union, Q load, O store), in blocks.
 CTA_OVERHEAD_BLOCKS = 1.0
 
 
+class CtaCosts(typing.NamedTuple):
+    """Costs of the exact kernel's CTAs, in K/V blocks run (CPU float64).
+
+    ``units``: [B, Hkv, U, nb], the CTA of unit u at query tile t: a head pair's union (the
+    two-tile kernel, U = G // 2) or one head (the one-tile kernel, U = G). ``odd_own`` and
+    ``odd_union``: [B, Hkv, nb] for the two-tile kernel when G is odd, the last head's block
+    count at tile t and the union of its tiles t and t - 1 (the CTA that runs both), else None.
+    """
+    units: torch.Tensor
+    odd_own: typing.Optional[torch.Tensor] = None
+    odd_union: typing.Optional[torch.Tensor] = None
+
+
 def cta_costs(selected, group, paired=True):
-    """Cost of each CTA of the exact kernel, [B, Hkv, units, nb] (CPU float64), in blocks: the
-    union of the block lists of the heads it holds. ``paired``: the two-tile kernel (head
-    pairs per CTA, csrc/attn_tc.cu); else one head per CTA (csrc/attn_tc1.cu)."""
+    """``CtaCosts`` of ``selected`` [B, nb, nb, H] (the routed block mask). ``paired``: the
+    two-tile kernel (csrc/attn_tc.cu: head pairs of a KV group at one tile, and the odd head
+    at two neighbouring tiles); else one head per CTA (csrc/attn_tc1.cu)."""
     b, nb, _, heads = selected.shape
     hkv = heads // group
     sel = selected.view(b, nb, nb, hkv, group)
+    per_tile = lambda m: m.sum(2).to(torch.float64).cpu()  # [B, nb, Hkv]
     if not paired:
-        return sel.sum(2).permute(0, 2, 3, 1).to(torch.float64).cpu()
-    pairs = (group + 1) // 2
-    out = torch.zeros(b, hkv, pairs, nb, dtype=torch.float64)
-    for j in range(pairs):
-        union, weight = sel[..., 2 * j], SINGLE_HEAD_CTA_WEIGHT
-        if 2 * j + 1 < group:
-            union, weight = union | sel[..., 2 * j + 1], 1.0
-        out[:, :, j, :] = (union.sum(2).to(torch.float64) * weight).permute(0, 2, 1).cpu()
+        return CtaCosts(sel.sum(2).permute(0, 2, 3, 1).to(torch.float64).cpu())
+    units = torch.zeros(b, hkv, group // 2, nb, dtype=torch.float64)
+    for j in range(group // 2):
+        units[:, :, j, :] = per_tile(sel[..., 2 * j] | sel[..., 2 * j + 1]).permute(0, 2, 1)
+    if group % 2 == 0:
+        return CtaCosts(units)
+    last = sel[..., group - 1]  # [B, nb (query tile), nb (key block), Hkv]
+    prev = torch.cat([torch.zeros_like(last[:, :1]), last[:, :-1]], dim=1)  # tile t - 1's row at t
+    return CtaCosts(units, per_tile(last).permute(0, 2, 1), per_tile(last | prev).permute(0, 2, 1))
+
+
+def launch_order(costs, kv_range, tile_range):
+    """The exact kernel's CTA costs for one shard in launch order (csrc/attn_tc.cu
+    ``exact_unit``; batch slowest, then the tiles longest first, then KV group and unit)."""
+    t0, t1 = tile_range
+    kv0, kv1 = kv_range
+    tiles = list(range(t1 - 1, t0 - 1, -1))
+    out = []
+    for b in range(costs.units.shape[0]):
+        unit_rows = costs.units[b, kv0:kv1].permute(2, 0, 1).reshape(costs.units.shape[3], -1).tolist()
+        if costs.odd_own is None:
+            for t in tiles:
+                out += unit_rows[t]
+            continue
+        own = costs.odd_own[b, kv0:kv1].t().tolist()
+        union = costs.odd_union[b, kv0:kv1].t().tolist()
+        for y in range(0, len(tiles), 2):
+            ta = tiles[y]
+            out += unit_rows[ta]
+            if y + 1 < len(tiles):
+                out += union[ta]
+                out += unit_rows[tiles[y + 1]]
+            else:
+                out += [c * LONE_TILE_CTA_WEIGHT for c in own[ta]]
     return out
 
 
 def makespan(costs, kv_range, tile_range, sms):
     """List-schedules the exact kernel's grid on ``sms`` SMs, one CTA per SM, in launch order
-    (x: KV group x head unit, fastest; y: the tiles, longest first; z: batch) and returns when
-    the last CTA ends, in blocks."""
+    and returns when the last CTA ends, in blocks."""
     import heapq
-    t0, t1 = tile_range
-    if t1 <= t0:
+    if tile_range[1] <= tile_range[0]:
         return 0.0
-    c = costs[:, kv_range[0]:kv_range[1], :, t0:t1].flip(-1).permute(0, 3, 1, 2).reshape(-1).tolist()
     free = [0.0] * sms
-    for w in c:
+    for w in launch_order(costs, kv_range, tile_range):
         heapq.heappush(free, heapq.heappop(free) + w + CTA_OVERHEAD_BLOCKS)
     return max(free)
 
@@ -175,16 +214,20 @@ def makespan(costs, kv_range, tile_range, sms):
 def tile_cuts(costs, kv, parts, blocks, sms):
     """Query-tile cuts [0 = c0 < c1 < ... < c_parts = blocks] of KV group ``kv`` over ``parts``
     ranks. Two parts: the cut that minimises the slower rank's simulated makespan (so the late,
-    long tiles fill whole waves of CTAs instead of leaving a near-empty last wave); more parts:
-    equal shares of the summed cost."""
-    per_tile = costs[:, kv].sum(dim=(0, 1))
+    long tiles fill whole waves of CTAs instead of leaving a near-empty last wave), and among
+    those the one that leaves the two ranks closest; more parts: equal shares of the summed
+    cost."""
+    per_tile = costs.units[:, kv].sum(dim=(0, 1))
+    if costs.odd_own is not None:
+        per_tile = per_tile + costs.odd_own[:, kv].sum(0)
     if parts == 2:
         best = None
         for cut in range(1, blocks):
-            span = max(makespan(costs, (kv, kv + 1), (0, cut), sms),
-                       makespan(costs, (kv, kv + 1), (cut, blocks), sms))
-            if best is None or span < best[0]:
-                best = (span, cut)
+            early = makespan(costs, (kv, kv + 1), (0, cut), sms)
+            late = makespan(costs, (kv, kv + 1), (cut, blocks), sms)
+            key = (max(early, late), abs(early - late))
+            if best is None or key < best[0]:
+                best = (key, cut)
         return [0, best[1], blocks]
     cum = per_tile.cumsum(0)
     total = float(cum[-1])
@@ -213,7 +256,7 @@ def partition(rank, world, kv_heads, blocks, costs=None, sms=148):
     kv = rank // parts
     j = rank % parts
     if costs is None:
-        costs = torch.arange(1, blocks + 1, dtype=torch.float64).expand(1, kv_heads, 1, blocks)
+        costs = CtaCosts(torch.arange(1, blocks + 1, dtype=torch.float64).expand(1, kv_heads, 1, blocks))
     cuts = tile_cuts(costs, kv, parts, blocks, sms)
     return (kv, kv + 1), (cuts[j], cuts[j + 1])
 

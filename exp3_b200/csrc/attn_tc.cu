@@ -5,9 +5,13 @@
 // order with an online softmax in exp2 units, causal mask on the diagonal block, P rounded to
 // bf16 before P.V, bf16 output and natural-log LSE.
 //
-// One CTA runs two query tiles: heads hA = kv*G + 2*pair and hB = hA + 1 of one KV group at the
-// same query tile t, so every K/V block loaded serves both (GQA sharing inside the CTA; no
-// cluster multicast). 384 threads in three warpgroups:
+// One CTA runs two query tiles of one KV group that read nearly the same K/V blocks, so every
+// block loaded serves both (GQA sharing inside the CTA; no cluster multicast): heads
+// hA = kv*G + 2*pair and hA + 1 at the same query tile t, or, for the last head of an odd
+// group, that head at tiles t and t - 1. A CTA holding one tile runs the same per-block chain
+// as a pair (the softmax, then the tile's own products), so pairing the odd head across
+// neighbouring tiles removes a whole CTA's worth of time per two tiles. 384 threads in three
+// warpgroups:
 //   warps 0..3   softmax of tile A       warps 4..7   softmax of tile B
 //   warp 8       TMA: Q, then the K ring warp 10      TMA: the V ring
 //   warp 9       MMA issuer (one elected lane)        warp 11 idle
@@ -93,26 +97,61 @@ FPX_INLINE uint32_t sw128_offset(int row, int col) {
 
 }  // namespace
 
+// The launch order of the work units: per two tiles (longest first) the U = kv_count * G/2 head
+// pairs of the longer tile, then (G odd) the kv_count units of the last head at both tiles,
+// then the U head pairs of the shorter tile. Returns the unit's two (tile, head) and whether
+// the second exists.
+struct ExactUnit {
+  int kvh, t[2], h[2];
+  bool has_b;
+};
+FPX_INLINE ExactUnit exact_unit(int idx, int tile_begin, int tiles, int kv_begin, int kv_count, int G) {
+  const int full = G / 2, U = kv_count * full, V = (G & 1) ? kv_count : 0;
+  const int j = idx / (2 * U + V), r = idx % (2 * U + V);
+  const int y = r < U + V ? 2 * j : 2 * j + 1;
+  const int slot = r < U + V ? r : r - (U + V);
+  const int t0 = tile_begin + tiles - 1 - y;
+  ExactUnit e;
+  if (slot < U) {
+    e.kvh = kv_begin + slot / full;
+    e.h[0] = e.kvh * G + 2 * (slot % full);
+    e.h[1] = e.h[0] + 1;
+    e.t[0] = e.t[1] = t0;
+    e.has_b = true;
+  } else {
+    e.kvh = kv_begin + (slot - U);
+    e.h[0] = e.h[1] = e.kvh * G + G - 1;
+    e.has_b = t0 - 1 >= tile_begin;
+    e.t[0] = t0;
+    e.t[1] = e.has_b ? t0 - 1 : t0;  // an absent tile keeps a valid index
+  }
+  return e;
+}
+__host__ __device__ inline int exact_units(int tiles, int kv_count, int G) {
+  return tiles * kv_count * (G / 2) + ((tiles + 1) / 2) * ((G & 1) ? kv_count : 0);
+}
+
 template <int kEmu>
 __global__ void __launch_bounds__(kThreads, 1)
     exact_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                    ExactParams p, int pairs) {
+                    ExactParams p, int tiles, int kv_count) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   Smem &sh = *reinterpret_cast<Smem *>(smem_raw + pad);
   volatile int *abort = &sh.abort;
 
-  // x: (KV group, head pair), fastest; y: tile, longest first; z: batch. The hardware starts
-  // CTAs in x-fastest order, so the whole grid runs longest tile first, and the head pairs of a
-  // KV group read the same K/V blocks at about the same time.
-  const int t = p.tile_begin + (gridDim.y - 1 - blockIdx.y);
-  const int pair = blockIdx.x % pairs;
-  const int kvh = p.head_begin / p.group + blockIdx.x / pairs;
+  // x: the work unit in launch order (longest tiles first, a KV group's units side by side, so
+  // they read the same K/V blocks at about the same time); z: batch.
+  const ExactUnit unit = exact_unit(blockIdx.x, p.tile_begin, tiles, p.head_begin / p.group, kv_count, p.group);
+  const int kvh = unit.kvh;
   const int b = blockIdx.z;
-  const int hA = kvh * p.group + 2 * pair;
-  const bool has_b = 2 * pair + 1 < p.group;
-  const int heads[2] = {hA, hA + 1};
+  const int hA = unit.h[0];
+  const bool has_b = unit.has_b;
+  // Tile x's head and query tile (128 rows), chosen by select so that nothing goes to local memory.
+  const int hB = unit.h[1], tA = unit.t[0], tB = unit.t[1];
+  auto head_of = [&](int x) { return x ? hB : hA; };
+  auto tile_of = [&](int x) { return x ? tB : tA; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool failed = *reinterpret_cast<volatile int *>(&g_device_error) != 0;
   // Block lists: the fused path's compact lists, or the reference's [B, nb, nb, H] int64
@@ -124,9 +163,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int32_t *lists[2];
   for (int x = 0; x < 2; ++x) {
     const bool live = x == 0 || has_b;
-    const int h = live ? heads[x] : hA;
-    const int64_t rr = ref ? 0 : p.route.row(b, h, t, p.H);
-    cnt[x] = (live && !failed) ? (ref ? p.ref_counts[((int64_t)b * nb + t) * p.H + h] : p.route.counts[rr]) : 0;
+    const int h = live ? head_of(x) : hA, tx = live ? tile_of(x) : tA;
+    const int64_t rr = ref ? 0 : p.route.row(b, h, tx, p.H);
+    cnt[x] = (live && !failed) ? (ref ? p.ref_counts[((int64_t)b * nb + tx) * p.H + h] : p.route.counts[rr]) : 0;
     cnt[x] = min(max(cnt[x], 0), nb);
     lists[x] = ref ? nullptr : p.route.lists + rr * p.route.nb;
   }
@@ -159,8 +198,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   for (int x = 0; x < 2; ++x)
     for (int i = threadIdx.x; i < cnt[x]; i += kThreads) {
-      const int blk = ref ? (int)p.ref_indices[(((int64_t)b * nb + t) * nb + i) * p.H + heads[x]] : lists[x][i];
-      if (blk >= 0 && blk <= t) atomicOr(&sh.bits[x][blk >> 5], 1u << (blk & 31));
+      const int blk = ref ? (int)p.ref_indices[(((int64_t)b * nb + tile_of(x)) * nb + i) * p.H + head_of(x)] : lists[x][i];
+      if (blk >= 0 && blk <= tile_of(x)) atomicOr(&sh.bits[x][blk >> 5], 1u << (blk & 31));
     }
   __syncthreads();
   if (warp == 8) {  // union of the two lists, ascending, with per-tile flags
@@ -194,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       nx = __reduce_add_sync(0xffffffffu, nx);
       if (lane == 0) {
         sh.n_tile[x] = nx;
-        sh.diag_tile[x] = (sh.bits[x][t >> 5] >> (t & 31)) & 1u;
+        sh.diag_tile[x] = (sh.bits[x][tile_of(x) >> 5] >> (tile_of(x) & 31)) & 1u;
       }
     }
   }
@@ -219,8 +258,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (is_k && lane == 0) {
           mbar_expect_tx(&sh.q_full, kTile * n_tiles);
           for (int x = 0; x < n_tiles; ++x) {
-            tma_load_4d(sh.q[x], &tm_q, &sh.q_full, 0, heads[x], t * 128, b);
-            tma_load_4d(sh.q[x] + kHalf, &tm_q, &sh.q_full, 64, heads[x], t * 128, b);
+            tma_load_4d(sh.q[x], &tm_q, &sh.q_full, 0, head_of(x), tile_of(x) * 128, b);
+            tma_load_4d(sh.q[x] + kHalf, &tm_q, &sh.q_full, 64, head_of(x), tile_of(x) * 128, b);
           }
         }
         for (int u = 0; u < n_union; ++u) {
@@ -308,9 +347,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_addr = tmem + lane_off + 128 * x;
     const uint32_t o_addr = tmem + lane_off + 256 + 128 * x;
     const bool live = x == 0 || has_b;
-    const int h = heads[x];
+    const int h = head_of(x);
     const int n = sh.n_tile[x];
-    const int qrow = t * 128 + r;
+    const int qrow = tile_of(x) * 128 + r;
     const float sl2 = p.scale_log2;
     // Blocks run in ascending order and end at most at t, so only the last can be the diagonal.
     const bool last_is_diag = n > 0 && sh.diag_tile[x];
@@ -397,8 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async();
       named_sync(1 + x, 128);
       if (r == 0 && !*abort) {
-        tma_store_4d(&tm_o, sh.q[x], 0, h, t * 128, b);
-        tma_store_4d(&tm_o, sh.q[x] + kHalf, 64, h, t * 128, b);
+        tma_store_4d(&tm_o, sh.q[x], 0, h, tile_of(x) * 128, b);
+        tma_store_4d(&tm_o, sh.q[x] + kHalf, 64, h, tile_of(x) * 128, b);
         bulk_commit();
         bulk_wait0();
       }
@@ -455,9 +494,9 @@ namespace {
 
 template <int kEmu>
 void launch_variant(dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap &tq, const CUtensorMap &tk,
-                    const CUtensorMap &tv, const CUtensorMap &to, const ExactParams &p, int pairs) {
+                    const CUtensorMap &tv, const CUtensorMap &to, const ExactParams &p, int tiles, int kv_count) {
   cudaFuncSetAttribute(exact_tc_kernel<kEmu>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  exact_tc_kernel<kEmu><<<grid, kThreads, smem, s>>>(tq, tk, tv, to, p, pairs);
+  exact_tc_kernel<kEmu><<<grid, kThreads, smem, s>>>(tq, tk, tv, to, p, tiles, kv_count);
 }
 
 }  // namespace
@@ -473,13 +512,13 @@ int launch_exact_tc(const ExactParams &p, int B, int L, int Hkv, int tiles, int 
       !encode_4d(&tv, p.v, kHeadDim, Hkv, L, B, p.v_sh, p.v_sl, p.v_sb) ||
       !encode_4d(&to, p.out, kHeadDim, p.H, L, B, p.o_sh, p.o_sl, p.o_sb))
     return FPX_ERR_INVALID;
-  const int pairs = (p.group + 1) / 2;
-  const dim3 grid((heads / p.group) * pairs, tiles, B);
+  const int kv_count = heads / p.group;
+  const dim3 grid(exact_units(tiles, kv_count, p.group), 1, B);
   const size_t smem = exact_tc_smem();
   switch (get_option(kOptExpEmulation)) {
-    case 0: launch_variant<0>(grid, smem, s, tq, tk, tv, to, p, pairs); break;
-    case 3: launch_variant<3>(grid, smem, s, tq, tk, tv, to, p, pairs); break;
-    default: launch_variant<2>(grid, smem, s, tq, tk, tv, to, p, pairs); break;
+    case 0: launch_variant<0>(grid, smem, s, tq, tk, tv, to, p, tiles, kv_count); break;
+    case 3: launch_variant<3>(grid, smem, s, tq, tk, tv, to, p, tiles, kv_count); break;
+    default: launch_variant<2>(grid, smem, s, tq, tk, tv, to, p, tiles, kv_count); break;
   }
   FPX_CHECK_LAUNCH();
   return FPX_OK;

@@ -89,9 +89,10 @@ def test_world_sizes_that_leave_work_unowned_are_refused():
 
 
 def test_tile_cut_fills_whole_waves():
-    """Config 2 at 8 ranks (two ranks per KV group): the simulated CTA schedule of the chosen cut
-    finishes no later than the causal-work median cut (tile 181 of 256), whose late rank leaves a
-    near-empty third wave of long tiles."""
+    """Config 2 at 8 ranks (two ranks per KV group): the chosen cut is the one whose simulated
+    CTA schedule ends first, so it finishes no later than the causal-work median cut (tile 181
+    of 256); and the schedule walks exactly the exact kernel's grid (3 head pairs per tile and
+    the odd head's CTA per two tiles)."""
     import torch
     bench = _bench_module()
     nb, group, heads = 256, 7, 28
@@ -101,6 +102,13 @@ def test_tile_cut_fills_whole_waves():
     assert c0 == 0
     span = lambda cut: max(bench.makespan(costs, (0, 1), (0, cut), 148), bench.makespan(costs, (0, 1), (cut, nb), 148))
     assert span(c1) <= span(181)
-    assert span(c1) < 0.95 * span(181)
+    assert span(c1) == min(span(cut) for cut in range(1, nb))
+    for t0, t1 in ((0, nb), (c1, nb), (3, 8)):
+        tiles = t1 - t0
+        assert len(bench.launch_order(costs, (0, 4), (t0, t1))) == 4 * (3 * tiles + (tiles + 1) // 2)
+    # the odd head's CTA holds tiles t and t - 1 (the union of their lists), and the lowest tile
+    # of an odd range alone
+    assert bench.launch_order(costs, (0, 1), (3, 6)) == [6.0] * 3 + [6.0] + [5.0] * 3 + [4.0] * 3 + [
+        4.0 * bench.LONE_TILE_CTA_WEIGHT]
     # the two ranks of a group share its tiles exactly
     assert bench.partition(1, 8, 4, nb, costs=costs, sms=148) == ((0, 1), (c1, nb))
