@@ -89,6 +89,22 @@ FPX_INLINE uint64_t desc_kmajor(const uint8_t *tile, int kk) {
 FPX_INLINE uint64_t desc_v(const uint8_t *tile, int kk) {
   return smem_desc_sw128(smem_u32(tile) + kk * 2048, kHalf, 1024);
 }
+// A shared-memory operand descriptor keeps the operand's address / 16 in its low 14 bits. Every
+// operand here lies below 2^18 bytes, so moving one by a byte offset adds offset / 16 to the low
+// word and leaves the other fields alone. The issuer keeps one low word per buffer and adds the
+// K-step's constant: one integer add per operand in front of each product instead of rebuilding
+// the descriptor, which, measured, is what held one thread to a product every ~95 cycles (65
+// with the descriptors ready, the tensor core's own rate).
+FPX_INLINE uint64_t desc_join(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+FPX_INLINE uint32_t desc_lo(uint64_t d) { return (uint32_t)d; }
+FPX_INLINE uint32_t desc_hi(uint64_t d) { return (uint32_t)(d >> 32); }
+// Low-word steps of K-step kk: K-major (Q, K) and MN-major V, as desc_kmajor / desc_v place them.
+constexpr uint32_t kmajor_step(int kk) { return (uint32_t)(((kk >> 2) * kHalf + (kk & 3) * 32) >> 4); }
+constexpr uint32_t v_step(int kk) { return (uint32_t)(kk * 2048 >> 4); }
 // Byte offset of (row, col) inside a 128 x 128 bf16 SW128 K-major tile.
 FPX_INLINE uint32_t sw128_offset(int row, int col) {
   const int half = col >> 6, chunk = (col & 63) >> 3;
@@ -284,21 +300,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else if (warp == 9) {
       // ------------------------------------------------------------ MMA issuer (lane 0 alone)
-      // The issuing thread bounds the kernel (one product per ~100 cycles), so it runs alone,
-      // without warp votes, and waits for the K and V stages before it waits for P: a stage
-      // has landed long before P is written, so those waits stay off the softmax -> P.V ->
-      // QK^T chain.
+      // The issuing thread is on the critical path, so it runs alone, without warp votes,
+      // with every descriptor's fixed part computed here, and waits for the K and V stages
+      // before it waits for P: a stage has landed long before P is written, so those waits
+      // stay off the softmax -> P.V -> QK^T chain.
       if (lane == 0 && n_union > 0 && mbar_wait(&sh.q_full, 0, abort)) {
         int pend[2] = {-1, -1}, n_pv[2] = {0, 0};
+        static_assert(kKStages == 2 && kVStages == 2, "the stage bases below are chosen by select");
+        const uint32_t hi_km = desc_hi(desc_kmajor(sh.q[0], 0)), hi_v = desc_hi(desc_v(sh.v[0], 0));
+        const uint32_t q_lo0 = desc_lo(desc_kmajor(sh.q[0], 0)), q_lo1 = desc_lo(desc_kmajor(sh.q[1], 0));
+        const uint32_t k_lo0 = desc_lo(desc_kmajor(sh.k[0], 0)), k_lo1 = desc_lo(desc_kmajor(sh.k[1], 0));
+        const uint32_t v_lo0 = desc_lo(desc_v(sh.v[0], 0)), v_lo1 = desc_lo(desc_v(sh.v[1], 0));
         // P.V of tile x for its pending block; frees the V stage once no tile still needs it.
         auto flush = [&](int x) -> bool {
           const int u = pend[x], s = u % kVStages;
           if (!mbar_wait(&sh.v_full[s], (u / kVStages) & 1, abort)) return false;
           if (!mbar_wait(&sh.p_full[x], n_pv[x] & 1, abort)) return false;
           tc_fence_after();
+          const uint32_t v_lo = s ? v_lo1 : v_lo0, o_tm = tmem + 256 + 128 * x, p_tm = tmem + 128 * x;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            mma_ts(tmem + 256 + 128 * x, tmem + 128 * x + 8 * kk, desc_v(sh.v[s], kk), kIdescPV,
+            mma_ts(o_tm, p_tm + 8 * kk, desc_join(v_lo + v_step(kk), hi_v), kIdescPV,
                    (n_pv[x] > 0 || kk > 0) ? 1u : 0u);
           tc_commit(&sh.o_done[x]);
           if (pend[x ^ 1] != u) tc_commit(&sh.v_empty[s]);
@@ -318,10 +340,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!(flags & (1 << x))) continue;
             if (pend[x] >= 0 && !(ok = flush(x))) break;
             tc_fence_after();
+            const uint32_t q_lo = x ? q_lo1 : q_lo0, k_lo = s ? k_lo1 : k_lo0, s_tm = tmem + 128 * x;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
-              mma_ss(tmem + 128 * x, desc_kmajor(sh.q[x], kk), desc_kmajor(sh.k[s], kk), kIdescQK,
-                     kk > 0 ? 1u : 0u);
+              mma_ss(s_tm, desc_join(q_lo + kmajor_step(kk), hi_km), desc_join(k_lo + kmajor_step(kk), hi_km),
+                     kIdescQK, kk > 0 ? 1u : 0u);
             tc_commit(&sh.s_full[x]);
             pend[x] = u;
           }

@@ -1,7 +1,9 @@
 // Measures how fast tcgen05.mma (kind::f16, bf16 in, fp32 accumulate, M = 128) can be issued
-// and executed on one SM, by shape and by the number of issuing warps. It explains the exact
-// attention kernel's bound (csrc/attn_tc.cu): one thread issues a 128 x 128 x 16 product about
-// every 100 cycles whatever N is, while the tensor core needs 64 cycles for it.
+// and executed on one SM, by shape and by the number of issuing warps. With the descriptors
+// rebuilt before each product, one thread issues a 128 x 128 x 16 product about every 95 cycles
+// whatever N is, while the tensor core needs 64 cycles for it; with the descriptors computed
+// before the loop (rate_pre_kernel) one thread issues at the tensor core's rate. The exact
+// attention kernel (csrc/attn_tc.cu) issues the second way.
 //
 //   nvcc -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -I include -o mma_issue_rate mma_issue_rate.cu
 //   ./mma_issue_rate
@@ -76,6 +78,69 @@ __global__ void __launch_bounds__(128, 1) rate_kernel(int n, int N, int issuers,
   if (threadIdx.x < 32) tmem_dealloc(tmem, 512);
 }
 
+// The same products with every descriptor computed before the timed loop and the loop unrolled,
+// so the issuing thread runs little more than the tcgen05.mma instructions themselves.
+// kChains accumulators take consecutive products in turn (TMEM columns [128 c, 128 c + N));
+// kMode 0: all SS; 1: all TS; 2: SS and TS alternate (Q.K^T and P.V of two tiles).
+template <int kChains, int kMode>
+__global__ void __launch_bounds__(128, 1) rate_pre_kernel(int n, int N, long long *out) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  for (int i = threadIdx.x; i < (kABytes + kBBytes) / 4; i += blockDim.x)
+    reinterpret_cast<uint32_t *>(base)[i] = 0x3c003c00u ^ ((uint32_t)i * 2654435761u & 0x00ff00ffu);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 32) {
+    tmem_alloc(&tmem_base, 512);
+    tmem_relinquish();
+  }
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  if (threadIdx.x == 0) {
+    const uint32_t idesc = idesc_bf16(128, N, false);
+    const uint32_t sa = smem_u32(base), sb = smem_u32(base + kABytes), bhalf = (uint32_t)N * 128;
+    uint64_t da[8], db[8];
+    uint32_t ta[8];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      da[kk] = desc_k(sa, kk, 16384);
+      db[kk] = desc_k(sb, kk, bhalf);
+      ta[kk] = tmem + 448 + 8 * kk;
+    }
+    const long long t0 = clock64();
+    for (int i = 0; i < n; i += 8 * kChains) {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+        for (int c = 0; c < kChains; ++c) {
+          const uint32_t d = tmem + 128 * c;
+          const bool ts = kMode == 1 || (kMode == 2 && (c & 1));
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          if (ts)
+            mma_ts(d, ta[kk], db[kk], idesc, acc);
+          else
+            mma_ss(d, da[kk], db[kk], idesc, acc);
+        }
+    }
+    tc_commit(&bar);
+    mbar_wait(&bar, 0, &abort_flag);
+    out[blockIdx.x * 4] = clock64() - t0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x < 32) tmem_dealloc(tmem, 512);
+}
+
 }  // namespace
 
 int main() {
@@ -113,6 +178,35 @@ int main() {
     std::sort(per.begin(), per.end());
     const double cyc = per[sms / 2];
     printf("%-4s %5d %8d %18.1f %16.0f\n", c.ts ? "TS" : "SS", c.N, c.issuers, cyc, 2.0 * 128 * c.N * 16 / cyc);
+  }
+  // Precomputed descriptors, one issuing thread.
+  struct PreCase {
+    const char *name;
+    int N, chains, mode;
+    void (*kernel)(int, int, long long *);
+  };
+  const PreCase pre[] = {{"SS pre", 128, 1, 0, rate_pre_kernel<1, 0>}, {"SS pre", 64, 1, 0, rate_pre_kernel<1, 0>},
+                         {"SS pre", 256, 1, 0, rate_pre_kernel<1, 0>}, {"TS pre", 128, 1, 1, rate_pre_kernel<1, 1>},
+                         {"SS pre", 128, 2, 0, rate_pre_kernel<2, 0>}, {"SS/TS pre", 128, 2, 2, rate_pre_kernel<2, 2>},
+                         {"TS pre", 128, 2, 1, rate_pre_kernel<2, 1>}};
+  printf("%-10s %5s %7s %18s %16s\n", "op", "N", "chains", "cycles per product", "FLOP/cycle/SM");
+  for (const PreCase &c : pre) {
+    cudaFuncSetAttribute(c.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    std::vector<long long> h(sms * 4);
+    for (int rep = 0; rep < 2; ++rep) {
+      c.kernel<<<sms, 128, smem>>>(n, c.N, d_out);
+      const cudaError_t e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) {
+        printf("error: %s\n", cudaGetErrorString(e));
+        return 1;
+      }
+    }
+    cudaMemcpy(h.data(), d_out, h.size() * sizeof(long long), cudaMemcpyDeviceToHost);
+    std::vector<double> per;
+    for (int i = 0; i < sms; ++i) per.push_back(h[i * 4] / (double)n);
+    std::sort(per.begin(), per.end());
+    const double cyc = per[sms / 2];
+    printf("%-10s %5d %7d %18.1f %16.0f\n", c.name, c.N, c.chains, cyc, 2.0 * 128 * c.N * 16 / cyc);
   }
   cudaFree(d_out);
   return 0;
