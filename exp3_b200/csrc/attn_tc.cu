@@ -89,20 +89,7 @@ FPX_INLINE uint64_t desc_kmajor(const uint8_t *tile, int kk) {
 FPX_INLINE uint64_t desc_v(const uint8_t *tile, int kk) {
   return smem_desc_sw128(smem_u32(tile) + kk * 2048, kHalf, 1024);
 }
-// A shared-memory operand descriptor keeps the operand's address / 16 in its low 14 bits. Every
-// operand here lies below 2^18 bytes, so moving one by a byte offset adds offset / 16 to the low
-// word and leaves the other fields alone. The issuer keeps one low word per buffer and adds the
-// K-step's constant: one integer add per operand in front of each product instead of rebuilding
-// the descriptor, which, measured, is what held one thread to a product every ~95 cycles (65
-// with the descriptors ready, the tensor core's own rate).
-FPX_INLINE uint64_t desc_join(uint32_t lo, uint32_t hi) {
-  uint64_t d;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
-  return d;
-}
-FPX_INLINE uint32_t desc_lo(uint64_t d) { return (uint32_t)d; }
-FPX_INLINE uint32_t desc_hi(uint64_t d) { return (uint32_t)(d >> 32); }
-// Low-word steps of K-step kk: K-major (Q, K) and MN-major V, as desc_kmajor / desc_v place them.
+// Descriptor low-word steps (desc_join in tc.cuh) of K-step kk: K-major (Q, K) and MN-major V, as desc_kmajor / desc_v place them.
 constexpr uint32_t kmajor_step(int kk) { return (uint32_t)(((kk >> 2) * kHalf + (kk & 3) * 32) >> 4); }
 constexpr uint32_t v_step(int kk) { return (uint32_t)(kk * 2048 >> 4); }
 // Byte offset of (row, col) inside a 128 x 128 bf16 SW128 K-major tile.

@@ -77,6 +77,11 @@ FPX_INLINE uint64_t desc_k1(const uint8_t *stage, int kk) {
 FPX_INLINE uint64_t desc_v1(const uint8_t *stage, int kk) {
   return smem_desc_sw128(smem_u32(stage) + kk * 2048, kKvAtom, 1024);
 }
+// Descriptor low-word steps (desc_join in tc.cuh) of K-step kk, as desc_q1 / desc_k1 / desc_v1
+// place them.
+constexpr uint32_t q1_step(int kk) { return (uint32_t)(((kk >> 2) * kQAtom + (kk & 3) * 32) >> 4); }
+constexpr uint32_t k1_step(int kk) { return (uint32_t)(((kk >> 2) * kKvAtom + (kk & 3) * 32) >> 4); }
+constexpr uint32_t v1_step(int kk) { return (uint32_t)(kk * 2048 >> 4); }
 // Byte offset of (row, col) in the 128 x D output tile (swizzled 64-column atoms).
 FPX_INLINE uint32_t out_offset(int row, int col) {
   const int atom = col >> 6, chunk = (col & 63) >> 3;
@@ -255,6 +260,11 @@ __global__ void __launch_bounds__(kThreads1, 1)
     if (n > 0 && mbar_wait_warp(&sh.q_full, 0, abort)) {
       int j = 0;
       bool ok = true;
+      // Descriptors: fixed parts computed once; a ring stage moves the low word by its size.
+      const uint32_t hi_km = desc_hi(desc_q1(sh.q, 0)), hi_v = desc_hi(desc_v1(sh.ring[0], 0));
+      const uint32_t q_lo = desc_lo(desc_q1(sh.q, 0)), k_lo0 = desc_lo(desc_k1(sh.ring[0], 0));
+      const uint32_t v_lo0 = desc_lo(desc_v1(sh.ring[0], 0));
+      constexpr uint32_t kStageStep = Geo::kStageBytes >> 4;
       auto qk = [&](int i) {
         const int buf = i & 1;
         for (int half = 0; half < 2 && ok; ++half, ++j) {
@@ -262,9 +272,10 @@ __global__ void __launch_bounds__(kThreads1, 1)
           if (!(ok = mbar_wait_warp(&sh.full[s], (j / kStages) & 1, abort))) break;
           tc_fence_after();
           if (lane == 0) {
+            const uint32_t k_lo = k_lo0 + (uint32_t)s * kStageStep, s_tm = tmem + 128 * buf + 64 * half;
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk)
-              mma_ss(tmem + 128 * buf + 64 * half, desc_q1(sh.q, kk), desc_k1(sh.ring[s], kk), kIdescQK,
+              mma_ss(s_tm, desc_join(q_lo + q1_step(kk), hi_km), desc_join(k_lo + k1_step(kk), hi_km), kIdescQK,
                      kk > 0 ? 1u : 0u);
             tc_commit(&sh.empty[s]);
           }
@@ -283,9 +294,10 @@ __global__ void __launch_bounds__(kThreads1, 1)
           if (!(ok = mbar_wait_warp(&sh.full[s], (j / kStages) & 1, abort))) break;
           tc_fence_after();
           if (lane == 0) {
+            const uint32_t v_lo = v_lo0 + (uint32_t)s * kStageStep, p_tm = tmem + 128 * buf + 32 * half;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              mma_ts(tmem + 256, tmem + 128 * buf + 32 * half + 8 * kk, desc_v1(sh.ring[s], kk), Geo::kIdescPV,
+              mma_ts(tmem + 256, p_tm + 8 * kk, desc_join(v_lo + v1_step(kk), hi_v), Geo::kIdescPV,
                      (i > 0 || half > 0 || kk > 0) ? 1u : 0u);
             tc_commit(&sh.empty[s]);
           }

@@ -249,6 +249,20 @@ FPX_INLINE uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t
   d |= (uint64_t)2 << 61;
   return d;
 }
+
+// A shared-memory operand descriptor keeps the operand's address / 16 in its low 14 bits. Every
+// operand lies below 2^18 bytes, so moving one by a byte offset (a multiple of 16) adds offset /
+// 16 to the low word and leaves the other fields alone. An MMA issuer keeps one low word per
+// buffer and adds each K-step's constant: one integer add per operand in front of a product
+// instead of rebuilding the descriptor, which measured is what held one thread to a product
+// every ~95 cycles (65 with the descriptors ready, the tensor core's own rate).
+FPX_INLINE uint64_t desc_join(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+FPX_INLINE uint32_t desc_lo(uint64_t d) { return (uint32_t)d; }
+FPX_INLINE uint32_t desc_hi(uint64_t d) { return (uint32_t)(d >> 32); }
 // Instruction descriptor, kind::f16: bf16 A and B, fp32 D, M x N, A K-major, B K- or MN-major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
