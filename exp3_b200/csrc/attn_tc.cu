@@ -380,13 +380,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 128; ++c) sv[c] = c <= r ? sv[c] : -INFINITY;
       }
+      // Row max over the 128 columns: eight running maxima, two columns folded in per step.
       float mx[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) mx[c] = sv[c];
 #pragma unroll
-      for (int c = 8; c < 128; c += 16)
+      for (int c = 8; c < 120; c += 16)
 #pragma unroll
         for (int j = 0; j < 8; ++j) mx[j] = fmax3(mx[j], sv[c + j], sv[c + 8 + j]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx[j] = fmaxf(mx[j], sv[120 + j]);
       const float bmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7])) * sl2;
       const float mn = fmaxf(m, bmax);
       float corr = 1.f;
