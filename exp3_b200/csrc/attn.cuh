@@ -79,4 +79,40 @@ int launch_merge(const __nv_bfloat16 *exact_out, const float *exact_lse, const f
                  const float *mean_lse, int64_t rows, __nv_bfloat16 *out, float *lse,
                  cudaStream_t s, int d = kHeadDim);
 
+// The two-tile kernels' work units (attn_tc.cu, attn_tail_tc.cu): two query tiles of one KV group
+// that read nearly the same blocks, heads hA and hA + 1 at one tile, or the last head of an odd
+// group at tiles t and t - 1. Launch order: per two tiles (longest first) the U = kv_count * G/2
+// head pairs of the longer tile, then (G odd) the kv_count units of the last head at both
+// tiles, then the U head pairs of the shorter tile. Returns the unit's two (tile, head) and
+// whether the second exists.
+struct ExactUnit {
+  int kvh, t[2], h[2];
+  bool has_b;
+};
+FPX_INLINE ExactUnit exact_unit(int idx, int tile_begin, int tiles, int kv_begin, int kv_count, int G) {
+  const int full = G / 2, U = kv_count * full, V = (G & 1) ? kv_count : 0;
+  const int j = idx / (2 * U + V), r = idx % (2 * U + V);
+  const int y = r < U + V ? 2 * j : 2 * j + 1;
+  const int slot = r < U + V ? r : r - (U + V);
+  const int t0 = tile_begin + tiles - 1 - y;
+  ExactUnit e;
+  if (slot < U) {
+    e.kvh = kv_begin + slot / full;
+    e.h[0] = e.kvh * G + 2 * (slot % full);
+    e.h[1] = e.h[0] + 1;
+    e.t[0] = e.t[1] = t0;
+    e.has_b = true;
+  } else {
+    e.kvh = kv_begin + (slot - U);
+    e.h[0] = e.h[1] = e.kvh * G + G - 1;
+    e.has_b = t0 - 1 >= tile_begin;
+    e.t[0] = t0;
+    e.t[1] = e.has_b ? t0 - 1 : t0;  // an absent tile keeps a valid index
+  }
+  return e;
+}
+__host__ __device__ inline int exact_units(int tiles, int kv_count, int G) {
+  return tiles * kv_count * (G / 2) + ((tiles + 1) / 2) * ((G & 1) ? kv_count : 0);
+}
+
 }  // namespace fpx

@@ -13,8 +13,9 @@
 // is accumulated from Q . hi^T + Q . lo^T, so the logits carry ~16 mantissa bits of mean_K
 // rather than bf16's 8. P (bf16, as the exact path rounds it) multiplies the bf16 mean V.
 //
-// Structure as the exact kernel (attn_tc.cu): one CTA runs the tiles of two heads of one KV
-// group at the same query tile, sharing every chunk; 384 threads —
+// Structure as the exact kernel (attn_tc.cu), with its work units (exact_unit): one CTA runs
+// two tiles of one KV group, two heads at the same query tile or the last head of an odd group
+// at tiles t and t - 1, sharing every chunk; 384 threads —
 //   warps 0..3 / 4..7  softmax of tiles A / B (thread = query row = TMEM lane), then the merge
 //   warp 8  TMA: Q, then the mean-K ring (stage 0 = high halves, stage 1 = low halves)
 //   warp 9  MMA issuer      warp 10  TMA: the mean-V ring      warp 11  idle
@@ -102,7 +103,8 @@ FPX_INLINE float tail_row(const float (&sv)[128], float sl2, float neg, uint32_t
 __global__ void __launch_bounds__(kThreads, 1)
     mean_tail_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_mkh,
                         const __grid_constant__ CUtensorMap tm_mkl, const __grid_constant__ CUtensorMap tm_mv,
-                        const __grid_constant__ CUtensorMap tm_o, MeanParams p, int pairs, float scale_log2,
+                        const __grid_constant__ CUtensorMap tm_o, MeanParams p, int tiles, int kv_count,
+                        float scale_log2,
                         int *device_error) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -110,13 +112,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int *abort = &sh.abort;
 
   // x: (KV group, head pair), fastest; y: tile, longest tail first; z: batch.
-  const int t = p.tile_begin + (gridDim.y - 1 - blockIdx.y);
-  const int pair = blockIdx.x % pairs;
-  const int kvh = p.head_begin / p.group + blockIdx.x / pairs;
+  // The exact kernel's work units and launch order (exact_unit): a head pair at one tile, or the
+  // last head of an odd group at tiles t and t - 1, whose tails are nearly the same blocks.
+  const ExactUnit unit = exact_unit(blockIdx.x, p.tile_begin, tiles, p.head_begin / p.group, kv_count, p.group);
+  const int kvh = unit.kvh;
   const int b = blockIdx.z;
-  const int hA = kvh * p.group + 2 * pair;
-  const bool has_b = 2 * pair + 1 < p.group;
-  const int heads[2] = {hA, hA + 1};
+  const int hA = unit.h[0], hB = unit.h[1], tA = unit.t[0], tB = unit.t[1];
+  const bool has_b = unit.has_b;
+  auto head_of = [&](int x) { return x ? hB : hA; };
+  auto tile_of = [&](int x) { return x ? tB : tA; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int words = p.route.words;
   const bool failed = *reinterpret_cast<volatile int *>(device_error) != 0;
@@ -125,15 +129,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the diagonal always among them) is then below t + 1. A CTA whose tiles both have none
   // leaves before it touches the bitmaps or a barrier: the exact output stands.
   {
-    const int c_a = p.route.counts[p.route.row(b, hA, t, p.H)];
-    const int c_b = has_b ? p.route.counts[p.route.row(b, hA + 1, t, p.H)] : t + 1;
-    if (c_a >= t + 1 && c_b >= t + 1) return;
+    const int c_a = p.route.counts[p.route.row(b, hA, tA, p.H)];
+    const int c_b = has_b ? p.route.counts[p.route.row(b, hB, tB, p.H)] : tB + 1;
+    if (c_a >= tA + 1 && c_b >= tB + 1) return;
   }
 
   // Tail bits of both tiles, then the chunks that hold any tail column (ascending, with flags).
   for (int x = 0; x < 2; ++x) {
     const bool live = (x == 0 || has_b) && !failed;
-    const uint32_t *src = p.route.tail + p.route.row(b, live ? heads[x] : hA, t, p.H) * words;
+    const uint32_t *src = p.route.tail + p.route.row(b, live ? head_of(x) : hA, live ? tile_of(x) : tA, p.H) * words;
     for (int w = threadIdx.x; w < kMaxBlocks / 32; w += kThreads) sh.bits[x][w] = (live && w < words) ? src[w] : 0u;
   }
   __syncthreads();
@@ -194,8 +198,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (is_k && lane == 0) {
         mbar_expect_tx(&sh.q_full, kTile * n_tiles);
         for (int x = 0; x < n_tiles; ++x) {
-          tma_load_4d(sh.q[x], &tm_q, &sh.q_full, 0, heads[x], t * 128, b);
-          tma_load_4d(sh.q[x] + kHalf, &tm_q, &sh.q_full, 64, heads[x], t * 128, b);
+          tma_load_4d(sh.q[x], &tm_q, &sh.q_full, 0, head_of(x), tile_of(x) * 128, b);
+          tma_load_4d(sh.q[x] + kHalf, &tm_q, &sh.q_full, 64, head_of(x), tile_of(x) * 128, b);
         }
       }
       bool ok = true;
@@ -295,8 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_addr = tmem + lane_off + 128 * x;
     const uint32_t o_addr = tmem + lane_off + 256 + 128 * x;
     const bool live = x == 0 || has_b;
-    const int h = heads[x];
-    const int qrow = t * 128 + r;
+    const int h = head_of(x);
+    const int qrow = tile_of(x) * 128 + r;
     int n_x = 0;  // chunks of this tile (the same for the whole warpgroup)
     for (int u = 0; u < n_union; ++u) n_x += (sh.u_flags[u] >> x) & 1;
     float m = -INFINITY, l = 0.f;
@@ -361,8 +365,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) {
         if (r == 0) {
           mbar_expect_tx(&sh.oe_full[x], kTile);
-          tma_load_4d(sh.q[x], &tm_o, &sh.oe_full[x], 0, h, t * 128, b);
-          tma_load_4d(sh.q[x] + kHalf, &tm_o, &sh.oe_full[x], 64, h, t * 128, b);
+          tma_load_4d(sh.q[x], &tm_o, &sh.oe_full[x], 0, h, tile_of(x) * 128, b);
+          tma_load_4d(sh.q[x] + kHalf, &tm_o, &sh.oe_full[x], 64, h, tile_of(x) * 128, b);
         }
         if (!mbar_wait_warp(&sh.oe_full[x], 0, abort)) ok = false;
       }
@@ -397,8 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async();
       named_sync(1 + x, 128);
       if (r == 0 && ok && !*abort) {
-        tma_store_4d(&tm_o, sh.q[x], 0, h, t * 128, b);
-        tma_store_4d(&tm_o, sh.q[x] + kHalf, 64, h, t * 128, b);
+        tma_store_4d(&tm_o, sh.q[x], 0, h, tile_of(x) * 128, b);
+        tma_store_4d(&tm_o, sh.q[x] + kHalf, 64, h, tile_of(x) * 128, b);
         bulk_commit();
         bulk_wait0();
       }
@@ -434,11 +438,11 @@ int launch_mean_tail_tc(const MeanParams &p, int B, int tiles, int heads, cudaSt
       !encode_4d(&tmv, p.mv_hi, d, p.Hkv, mean_blocks, B, kHeadDim, dstride, bstride) ||
       !encode_4d(&to, p.out, d, p.H, p.L, B, p.o_sh, p.o_sl, p.o_sb))
     return FPX_ERR_INVALID;
-  const int pairs = (p.group + 1) / 2;
-  const dim3 grid((heads / p.group) * pairs, tiles, B);
+  const int kv_count = heads / p.group;
+  const dim3 grid(exact_units(tiles, kv_count, p.group), 1, B);
   const size_t smem = mean_tail_tc_smem();
   cudaFuncSetAttribute(mean_tail_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  mean_tail_tc_kernel<<<grid, kThreads, smem, s>>>(tq, tmkh, tmkl, tmv, to, p, pairs, p.scale * kLog2e,
+  mean_tail_tc_kernel<<<grid, kThreads, smem, s>>>(tq, tmkh, tmkl, tmv, to, p, tiles, kv_count, p.scale * kLog2e,
                                                    device_error);
   FPX_CHECK_LAUNCH();
   return FPX_OK;

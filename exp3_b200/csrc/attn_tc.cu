@@ -100,40 +100,6 @@ FPX_INLINE uint32_t sw128_offset(int row, int col) {
 
 }  // namespace
 
-// The launch order of the work units: per two tiles (longest first) the U = kv_count * G/2 head
-// pairs of the longer tile, then (G odd) the kv_count units of the last head at both tiles,
-// then the U head pairs of the shorter tile. Returns the unit's two (tile, head) and whether
-// the second exists.
-struct ExactUnit {
-  int kvh, t[2], h[2];
-  bool has_b;
-};
-FPX_INLINE ExactUnit exact_unit(int idx, int tile_begin, int tiles, int kv_begin, int kv_count, int G) {
-  const int full = G / 2, U = kv_count * full, V = (G & 1) ? kv_count : 0;
-  const int j = idx / (2 * U + V), r = idx % (2 * U + V);
-  const int y = r < U + V ? 2 * j : 2 * j + 1;
-  const int slot = r < U + V ? r : r - (U + V);
-  const int t0 = tile_begin + tiles - 1 - y;
-  ExactUnit e;
-  if (slot < U) {
-    e.kvh = kv_begin + slot / full;
-    e.h[0] = e.kvh * G + 2 * (slot % full);
-    e.h[1] = e.h[0] + 1;
-    e.t[0] = e.t[1] = t0;
-    e.has_b = true;
-  } else {
-    e.kvh = kv_begin + (slot - U);
-    e.h[0] = e.h[1] = e.kvh * G + G - 1;
-    e.has_b = t0 - 1 >= tile_begin;
-    e.t[0] = t0;
-    e.t[1] = e.has_b ? t0 - 1 : t0;  // an absent tile keeps a valid index
-  }
-  return e;
-}
-__host__ __device__ inline int exact_units(int tiles, int kv_count, int G) {
-  return tiles * kv_count * (G / 2) + ((tiles + 1) / 2) * ((G & 1) ? kv_count : 0);
-}
-
 template <int kEmu>
 __global__ void __launch_bounds__(kThreads, 1)
     exact_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
