@@ -5,6 +5,7 @@
 // Reference: upstream/flashprefill_native_forward.py:27-175, 357-417 (V1) and
 // kernels.py:22-176 (descriptors, selectors, selection, index/mask conversion).
 #include <algorithm>
+#include <cstdint>
 
 #include "attn.cuh"
 #include "route.cuh"
@@ -16,26 +17,10 @@ namespace fpx {
 // walks the block's valid rows in order, so the fp32 sums have a fixed sequential order
 // (the bf16 V1 mean is bf16(sum / n), see upstream:58-68; the fp32 descriptors follow
 // kernels.py:22-46).
-template <bool kBf16Mean, bool kDesc, int D = kHeadDim>
-__global__ void __launch_bounds__(D) block_stats_kernel(StatsParams p) {
-  const int blk = blockIdx.x, kvh = p.kv_begin + blockIdx.y, b = blockIdx.z;
-  const int c = threadIdx.x;
-  const int r0 = blk * kBlock;
-  const int n = min(kBlock, p.L - r0);
-  const __nv_bfloat16 *kp = p.k + b * p.k_sb + (int64_t)r0 * p.k_sl + kvh * p.k_sh + c;
-  const __nv_bfloat16 *vp = p.v + b * p.v_sb + (int64_t)r0 * p.v_sl + kvh * p.v_sh + c;
-  float sk = 0.f, sk2 = 0.f, sv = 0.f, sv2 = 0.f;
-#pragma unroll 8
-  for (int r = 0; r < n; ++r) {
-    const float x = __bfloat162float(kp[(int64_t)r * p.k_sl]);
-    sk = __fadd_rn(sk, x);
-    if (kDesc) {
-      sk2 = __fadd_rn(sk2, __fmul_rn(x, x));
-      const float y = __bfloat162float(vp[(int64_t)r * p.v_sl]);
-      sv = __fadd_rn(sv, y);
-      sv2 = __fadd_rn(sv2, __fmul_rn(y, y));
-    }
-  }
+// The statistics of one (block, KV head, batch) from its column sums (thread c: dimension c).
+template <bool kBf16Mean, bool kDesc, int D>
+__device__ __forceinline__ void block_stats_store(const StatsParams &p, int b, int blk, int kvh, int c, int n, float sk,
+                                                  float sk2, float sv, float sv2) {
   const float fn = (float)n;
   const int64_t o = (((int64_t)b * p.nb + blk) * p.Hkv + kvh) * D + c;
   if (kBf16Mean) p.mean_bf16[o] = __float2bfloat16_rn(__fdiv_rn(sk, fn));
@@ -65,26 +50,109 @@ __global__ void __launch_bounds__(D) block_stats_kernel(StatsParams p) {
   }
 }
 
+template <bool kBf16Mean, bool kDesc, int D = kHeadDim>
+__global__ void __launch_bounds__(D) block_stats_kernel(StatsParams p) {
+  const int blk = blockIdx.x, kvh = p.kv_begin + blockIdx.y, b = blockIdx.z;
+  const int c = threadIdx.x;
+  const int r0 = blk * kBlock;
+  const int n = min(kBlock, p.L - r0);
+  const __nv_bfloat16 *kp = p.k + b * p.k_sb + (int64_t)r0 * p.k_sl + kvh * p.k_sh + c;
+  const __nv_bfloat16 *vp = p.v + b * p.v_sb + (int64_t)r0 * p.v_sl + kvh * p.v_sh + c;
+  float sk = 0.f, sk2 = 0.f, sv = 0.f, sv2 = 0.f;
+#pragma unroll 8
+  for (int r = 0; r < n; ++r) {
+    const float x = __bfloat162float(kp[(int64_t)r * p.k_sl]);
+    sk = __fadd_rn(sk, x);
+    if (kDesc) {
+      sk2 = __fadd_rn(sk2, __fmul_rn(x, x));
+      const float y = __bfloat162float(vp[(int64_t)r * p.v_sl]);
+      sv = __fadd_rn(sv, y);
+      sv2 = __fadd_rn(sv2, __fmul_rn(y, y));
+    }
+  }
+  block_stats_store<kBf16Mean, kDesc, D>(p, b, blk, kvh, c, n, sk, sk2, sv, sv2);
+}
+
+// The same statistics with the block's rows staged through shared memory, kStageRows at a time:
+// the whole stage is loaded at once by 16-byte coalesced loads, then thread c adds column c's
+// rows in order, so every sum is the one the per-column walk above gives. For rows whose
+// element strides are multiples of 8 and 16-byte aligned bases.
+template <bool kBf16Mean, bool kDesc, int D = kHeadDim>
+__global__ void __launch_bounds__(D) block_stats_staged_kernel(StatsParams p) {
+  constexpr int kStageRows = D == 256 ? 32 : 64, kVecs = D / 8;  // 16-byte vectors per row
+  __shared__ __align__(16) __nv_bfloat16 ks[kStageRows][D];
+  __shared__ __align__(16) __nv_bfloat16 vs[kDesc ? kStageRows : 1][D];
+  const int blk = blockIdx.x, kvh = p.kv_begin + blockIdx.y, b = blockIdx.z;
+  const int c = threadIdx.x;
+  const int r0 = blk * kBlock;
+  const int n = min(kBlock, p.L - r0);
+  const __nv_bfloat16 *kb = p.k + b * p.k_sb + (int64_t)r0 * p.k_sl + kvh * p.k_sh;
+  const __nv_bfloat16 *vb = p.v + b * p.v_sb + (int64_t)r0 * p.v_sl + kvh * p.v_sh;
+  float sk = 0.f, sk2 = 0.f, sv = 0.f, sv2 = 0.f;
+  for (int base = 0; base < n; base += kStageRows) {
+    const int rows = min(kStageRows, n - base);
+#pragma unroll 4
+    for (int e = c; e < rows * kVecs; e += D) {
+      const int rr = e / kVecs, cv = e % kVecs;
+      reinterpret_cast<uint4 *>(&ks[rr][0])[cv] =
+          *reinterpret_cast<const uint4 *>(kb + (int64_t)(base + rr) * p.k_sl + 8 * cv);
+      if (kDesc)
+        reinterpret_cast<uint4 *>(&vs[rr][0])[cv] =
+            *reinterpret_cast<const uint4 *>(vb + (int64_t)(base + rr) * p.v_sl + 8 * cv);
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int r = 0; r < rows; ++r) {
+      const float x = __bfloat162float(ks[r][c]);
+      sk = __fadd_rn(sk, x);
+      if (kDesc) {
+        sk2 = __fadd_rn(sk2, __fmul_rn(x, x));
+        const float y = __bfloat162float(vs[r][c]);
+        sv = __fadd_rn(sv, y);
+        sv2 = __fadd_rn(sv2, __fmul_rn(y, y));
+      }
+    }
+    __syncthreads();
+  }
+  block_stats_store<kBf16Mean, kDesc, D>(p, b, blk, kvh, c, n, sk, sk2, sv, sv2);
+}
+
+// 16-byte vector loads are legal for rows with element strides that are multiples of 8 from a
+// 16-byte aligned base.
+static bool rows_vectorizable(const void *base, int64_t sb, int64_t sl, int64_t sh) {
+  return (reinterpret_cast<uintptr_t>(base) & 15u) == 0 && sb % 8 == 0 && sl % 8 == 0 && sh % 8 == 0;
+}
+
+template <int D>
+static void launch_block_stats_d(const StatsParams &p, dim3 grid, bool bf16_mean, bool desc, bool staged,
+                                 cudaStream_t s) {
+  if (staged) {
+    if (bf16_mean && desc)
+      block_stats_staged_kernel<true, true, D><<<grid, D, 0, s>>>(p);
+    else if (bf16_mean)
+      block_stats_staged_kernel<true, false, D><<<grid, D, 0, s>>>(p);
+    else if (desc)
+      block_stats_staged_kernel<false, true, D><<<grid, D, 0, s>>>(p);
+    return;
+  }
+  if (bf16_mean && desc)
+    block_stats_kernel<true, true, D><<<grid, D, 0, s>>>(p);
+  else if (bf16_mean)
+    block_stats_kernel<true, false, D><<<grid, D, 0, s>>>(p);
+  else if (desc)
+    block_stats_kernel<false, true, D><<<grid, D, 0, s>>>(p);
+}
+
 int launch_block_stats(const StatsParams &p, int blocks, int kv_count, int B, bool bf16_mean,
                        bool desc, cudaStream_t s) {
   if (blocks <= 0 || kv_count <= 0) return FPX_OK;
   dim3 grid(blocks, kv_count, B);
-  if (p.d == 256) {  // head dim 256 (check_qwen35_math.py): one thread per dimension
-    if (bf16_mean && desc)
-      block_stats_kernel<true, true, 256><<<grid, 256, 0, s>>>(p);
-    else if (bf16_mean)
-      block_stats_kernel<true, false, 256><<<grid, 256, 0, s>>>(p);
-    else if (desc)
-      block_stats_kernel<false, true, 256><<<grid, 256, 0, s>>>(p);
-    FPX_CHECK_LAUNCH();
-    return FPX_OK;
-  }
-  if (bf16_mean && desc)
-    block_stats_kernel<true, true><<<grid, 128, 0, s>>>(p);
-  else if (bf16_mean)
-    block_stats_kernel<true, false><<<grid, 128, 0, s>>>(p);
-  else if (desc)
-    block_stats_kernel<false, true><<<grid, 128, 0, s>>>(p);
+  const bool staged = rows_vectorizable(p.k, p.k_sb, p.k_sl, p.k_sh) &&
+                      (!desc || rows_vectorizable(p.v, p.v_sb, p.v_sl, p.v_sh));
+  if (p.d == 256)  // head dim 256 (check_qwen35_math.py): one thread per dimension
+    launch_block_stats_d<256>(p, grid, bf16_mean, desc, staged, s);
+  else
+    launch_block_stats_d<128>(p, grid, bf16_mean, desc, staged, s);
   FPX_CHECK_LAUNCH();
   return FPX_OK;
 }
