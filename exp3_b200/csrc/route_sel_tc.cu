@@ -30,9 +30,10 @@
 // One CTA per (b, h, t); 384 threads:
 //   warp 0       TMA: Q, then the operand ring (chunk by chunk: mean-K hi, lo, var-K hi, lo)
 //   warp 1       MMA issuer (one lane), TMEM owner
-//   warps 2..3   square Q into Q2hi / Q2lo (same swizzled layout: squaring is elementwise)
-//   warps 4..11  epilogue, two warpgroups splitting each chunk's columns (pass 1) or rows
-//                (pass 2); then warpgroup 0 runs the selection
+//   warps 2..11  first square Q into Q2hi / Q2lo together (same swizzled layout: squaring is
+//                elementwise; the var-K products wait for it)
+//   warps 4..11  then the epilogue, two warpgroups splitting each chunk's columns (pass 1) or
+//                rows (pass 2); then warpgroup 0 runs the selection
 // TMEM: two buffers x (logit accumulator, u accumulator) x 128 columns.
 // Waits are bounded; a failed wait flags the CTA and the device error word and the row is
 // written with count 0.
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sh.q_full, 1);
-    mbar_init(&sh.q2_full, 64);
+    mbar_init(&sh.q2_full, kThreads - 64);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sh.r_full[s], 1);
       mbar_init(&sh.r_empty[s], 1);
@@ -219,13 +220,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       mbar_wait(&sh.drain, 0, &never);
     }
-  } else if (warp < 4) {
+  } else {
     // ------------------------------------------------------------------ Q^2 = hi + lo
+    // Warps 2..11 together: the epilogue warps have nothing to do until pass 1's first
+    // accumulators, and the var-K products wait for Q^2.
     if (kSel > 0 && chunks > 0) {
       const bool ok = mbar_wait(&sh.q_full, 0, abort);
       if (ok) {
         const int tid = threadIdx.x - 64;
-        for (int i = tid; i < (int)(kTile / 16); i += 64) {
+        for (int i = tid; i < (int)(kTile / 16); i += kThreads - 64) {
           const uint4 v = reinterpret_cast<const uint4 *>(sh.q)[i];
           const uint32_t *w = reinterpret_cast<const uint32_t *>(&v);
           uint4 hi4, lo4;
@@ -247,7 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async();  // generic writes -> read by the tensor core
       mbar_arrive(&sh.q2_full);
     }
-  } else {
+  }
+  if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue
     // Two warpgroups: in pass 1 group g reduces columns [64 g, 64 g + 64) of every chunk for
     // its row, in pass 2 rows [64 g, 64 g + 64) for its block; the halves meet in shared memory.
