@@ -62,6 +62,9 @@ struct MeanParams {
   const __nv_bfloat16 *k, *v;
   int64_t k_sb, k_sl, k_sh, v_sb, v_sl, v_sh;
   uint8_t *choice;
+  // rescue choice: fp32 query means [B][nb][H][d] filled by the choice launch itself (one pass
+  // over Q), or null to have each choice CTA form its group's means from Q
+  float *qmean;
   int d;                            // head dim: 128 (0 reads as 128) or 256 (block-mean tail only)
 };
 

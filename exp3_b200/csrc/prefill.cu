@@ -17,6 +17,7 @@ struct Workspace {
   __nv_bfloat16 *mk16, *mkh, *mkl, *mvh, *vkh, *vkl;
   uint8_t *choice;  // rescue token of every (b, h, t, kb), [B][H][nb][nb]
   float *mk, *mv, *vk, *sv, *lse;
+  float *qmean;     // rescue choice: fp32 query means, [B][nb][H][d]
   size_t bytes;
 };
 
@@ -47,6 +48,7 @@ static Workspace carve(void *base, int B, int L, int H, int Hkv, int d = kHeadDi
   w.sv = reinterpret_cast<float *>(take((size_t)B * nb * Hkv * 4));
   w.lse = reinterpret_cast<float *>(take((size_t)B * L * H * 4));
   w.choice = static_cast<uint8_t *>(take((size_t)B * H * nb * nb));
+  w.qmean = reinterpret_cast<float *>(take((size_t)B * nb * H * d * 4));
   w.bytes = off;
   return w;
 }
@@ -239,6 +241,7 @@ extern "C" int fpx_prefill_attention(int method, double alpha, int sink, int win
     mp.scale = (float)scale; mp.route = rv;
     mp.out = static_cast<__nv_bfloat16 *>(out); mp.o_sb = o_sb; mp.o_sl = o_sl; mp.o_sh = o_sh;
     mp.lse = lse_out; mp.d = d;
+    mp.qmean = ws.qmean;
     rc = launch_rescue_choice(mp, kMeanMergeInPlace, tiles, kv_count, B, s);
     if (rc) return rc;
     const int keys = method == FPX_METHOD_FP_V1_RESCUE_V2 ? 2 : 1;

@@ -5,9 +5,11 @@
 // (torch.argmax: the first maximum on ties). The tail tokens then enter the rescue tail through
 // mean_tail_kernel (mean.cu).
 //
-// kRescueSplits CTAs per (b, KV group, t), 256 threads each. Every CTA forms the group's query
-// means in shared memory (fp32 sums of the valid rows, then divided by the row count) and
-// compacts the union of the group's tails into a list; CTA s of the split takes list entries
+// kRescueSplits CTAs per (b, KV group, t), 256 threads each. On the fused path one pass over Q
+// first forms every (b, t, h)'s query mean (fp32 sums of the valid rows, then divided by the
+// row count) into the workspace and the split CTAs copy their group's means; otherwise each
+// CTA forms them (the same arithmetic). Every CTA compacts the union of the group's tails into
+// a list; CTA s of the split takes list entries
 // s, s + kRescueSplits, ... For each of its blocks, thread pair (2j, 2j + 1) holds token j's key
 // row in registers, 64 dimensions each (the next block's row is loaded while the current one is
 // reduced), and forms one dot product per head with the broadcast means; a (value, index)
@@ -19,6 +21,46 @@ namespace fpx {
 constexpr int kRescueMaxGroup = 16;
 constexpr int kRescueSplits = 4;
 constexpr int kChoiceThreads = 256;
+
+// The fp32 mean of query tile t's valid rows of head h (kernels.py:278-279) into dst[D], by 256
+// threads: warp w sums rows w, w + 8, ... for dimensions 4 lane + 128 c .. + 3, and the eight
+// partial sums are added in warp order before the division by the row count. `part` is [8][D]
+// of shared memory.
+template <int D>
+__device__ __forceinline__ void tile_query_mean(const MeanParams &p, int b, int t, int h, float *part, float *dst) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rows = min(kBlock, p.L - t * kBlock);
+#pragma unroll
+  for (int c = 0; c < D / 128; ++c) {
+    const __nv_bfloat16 *src = p.q + b * p.q_sb + (int64_t)t * kBlock * p.q_sl + h * p.q_sh + 4 * lane + 128 * c;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll 4
+    for (int r = warp; r < rows; r += 8) {
+      const uint2 u = *reinterpret_cast<const uint2 *>(src + (int64_t)r * p.q_sl);
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
+      const float2 cc = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
+      s0 += a.x; s1 += a.y; s2 += cc.x; s3 += cc.y;
+    }
+    *reinterpret_cast<float4 *>(part + warp * D + 4 * lane + 128 * c) = make_float4(s0, s1, s2, s3);
+  }
+  __syncthreads();
+  if (tid < D) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += part[w * D + tid];
+    dst[tid] = s / (float)rows;
+  }
+  __syncthreads();
+}
+
+// The query means of every (b, t, h) of the launch, once, for the choice CTAs to share.
+template <int D>
+__global__ void __launch_bounds__(256) rescue_qmean_kernel(MeanParams p) {
+  __shared__ __align__(16) float part[8 * D];
+  const int t = p.tile_begin + blockIdx.x, h = p.head_begin + blockIdx.y, b = blockIdx.z;
+  if (t == 0) return;  // tile 0 has no earlier block to rescue from
+  tile_query_mean<D>(p, b, t, h, part, p.qmean + (((int64_t)b * p.nb + t) * p.H + h) * D);
+}
 
 template <int kMode, int D = kHeadDim>
 __global__ void __launch_bounds__(256, D == kHeadDim ? 2 : 1) rescue_choice_kernel(MeanParams p) {
@@ -70,33 +112,14 @@ __global__ void __launch_bounds__(256, D == kHeadDim ? 2 : 1) rescue_choice_kern
   }
   __syncthreads();
   if (split >= nu) return;  // nothing for this CTA of the split (uniform)
-  // Query means (kernels.py:278-279): fp32 sums over the valid rows, then divided by the count.
-  // Warp w sums rows w, w + 8, ... for dimensions 4 lane + 128 c .. + 3; the eight partial sums
-  // are added in warp order.
-  const int rows = min(kBlock, p.L - t * kBlock);
-  for (int g = 0; g < G; ++g) {
-    const int h = kvh * G + g;
-#pragma unroll
-    for (int c = 0; c < D / 128; ++c) {
-      const __nv_bfloat16 *src = p.q + b * p.q_sb + (int64_t)t * kBlock * p.q_sl + h * p.q_sh + 4 * lane + 128 * c;
-      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll 4
-      for (int r = warp; r < rows; r += 8) {
-        const uint2 u = *reinterpret_cast<const uint2 *>(src + (int64_t)r * p.q_sl);
-        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
-        const float2 cc = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
-        s0 += a.x; s1 += a.y; s2 += cc.x; s3 += cc.y;
-      }
-      *reinterpret_cast<float4 *>(part + warp * D + 4 * lane + 128 * c) = make_float4(s0, s1, s2, s3);
-    }
+  // Query means (kernels.py:278-279): from the launch's shared pass when there is one, else
+  // formed here (the same arithmetic).
+  if (p.qmean) {
+    for (int i = tid; i < G * D; i += kChoiceThreads)
+      qm[i] = p.qmean[(((int64_t)b * p.nb + t) * p.H + kvh * G + i / D) * D + i % D];
     __syncthreads();
-    if (tid < D) {
-      float s = 0.f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) s += part[w * D + tid];
-      qm[g * D + tid] = s / (float)rows;
-    }
-    __syncthreads();
+  } else {
+    for (int g = 0; g < G; ++g) tile_query_mean<D>(p, b, t, kvh * G + g, part, qm + g * D);
   }
 
   // Thread pair (2 j, 2 j + 1) holds token j's key row, D / 2 dimensions each.
@@ -178,6 +201,13 @@ int launch_rescue_choice(const MeanParams &p, int mode, int tiles, int kv_count,
                       (size_t)p.group * ((p.nb + 31) / 32) * 4 + (size_t)((p.nb + 1) & ~1) * 2 + 32;
   if (smem > 200 * 1024) return FPX_ERR_UNSUPPORTED;
   const dim3 grid(tiles, kv_count, B * kRescueSplits);
+  if (p.qmean) {  // one pass over Q for the query means, shared by the choice CTAs
+    const dim3 mgrid(tiles, kv_count * p.group, B);
+    if (d == 256)
+      rescue_qmean_kernel<256><<<mgrid, kChoiceThreads, 0, s>>>(p);
+    else
+      rescue_qmean_kernel<kHeadDim><<<mgrid, kChoiceThreads, 0, s>>>(p);
+  }
 #define FPX_CHOICE_LAUNCH(MODE, DD)                                                                     \
   do {                                                                                                  \
     cudaFuncSetAttribute(rescue_choice_kernel<MODE, DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
