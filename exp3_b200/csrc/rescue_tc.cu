@@ -140,8 +140,9 @@ __global__ void __launch_bounds__(128) rescue_tail_tc_kernel(const __grid_consta
     const int nc = min(128, ntail - c0);
     // 1-2. gather, then S = Q K^T. The remainder pass runs it twice through the one K tile:
     // part 0 writes K_rest's high halves (and V_rest), part 1 its low halves, accumulated into
-    // S; thread j recomputes its slot's remainder for part 1 from the same (L2-resident) rows.
+    // S; thread j keeps its slot's low halves in registers from part 0.
     const int parts = rest ? 2 : 1;
+    uint32_t klo[64];  // the remainder pass: K_rest's low halves, kept from part 0 for part 1
     for (int part = 0; part < parts && ok; ++part) {
       const int j = tid;
       if (j < nc) {
@@ -149,12 +150,17 @@ __global__ void __launch_bounds__(128) rescue_tail_tc_kernel(const __grid_consta
         const int64_t tok = (int64_t)kb * kBlock + (choice[kb] & (kBlock - 1));
         const uint4 *krow = reinterpret_cast<const uint4 *>(p.k + b * p.k_sb + tok * p.k_sl + kvh * p.k_sh);
         const uint4 *vrow = reinterpret_cast<const uint4 *>(p.v + b * p.v_sb + tok * p.v_sl + kvh * p.v_sh);
-        if (rest) {
+        if (rest && part == 1) {
+#pragma unroll
+          for (int ch = 0; ch < 16; ++ch)
+            *reinterpret_cast<uint4 *>(sh.k + chunk_offset(j, ch)) =
+                make_uint4(klo[4 * ch], klo[4 * ch + 1], klo[4 * ch + 2], klo[4 * ch + 3]);
+        } else if (rest) {
           // (sum - rescue) / 127 with sum = 128 x mean (exact): the remainder's mean K / V
           const float4 *mk4 = reinterpret_cast<const float4 *>(mk_base + kb * dstride);
           const float4 *mv4 = reinterpret_cast<const float4 *>(mv_base + kb * dstride);
           auto rest_of = [](float mean, float x) { return __fdiv_rn(__fsub_rn(__fmul_rn(mean, 128.f), x), 127.f); };
-#pragma unroll 4
+#pragma unroll
           for (int ch = 0; ch < 16; ++ch) {
             const uint4 ku = krow[ch];
             const float4 ma = mk4[2 * ch], mb = mk4[2 * ch + 1];
@@ -166,10 +172,11 @@ __global__ void __launch_bounds__(128) rescue_tail_tc_kernel(const __grid_consta
               const float2 kx = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kw[e]));
               const float r0 = rest_of(mkv[2 * e], kx.x), r1 = rest_of(mkv[2 * e + 1], kx.y);
               const float h0 = __bfloat162float(__float2bfloat16_rn(r0)), h1 = __bfloat162float(__float2bfloat16_rn(r1));
-              kout[e] = part == 0 ? pack_bf16(h0, h1) : pack_bf16(__fsub_rn(r0, h0), __fsub_rn(r1, h1));
+              kout[e] = pack_bf16(h0, h1);
+              klo[4 * ch + e] = pack_bf16(__fsub_rn(r0, h0), __fsub_rn(r1, h1));
             }
             *reinterpret_cast<uint4 *>(sh.k + chunk_offset(j, ch)) = make_uint4(kout[0], kout[1], kout[2], kout[3]);
-            if (part == 0) {
+            {
               const uint4 vu = vrow[ch];
               const float4 va = mv4[2 * ch], vb = mv4[2 * ch + 1];
               const uint32_t vw[4] = {vu.x, vu.y, vu.z, vu.w};
