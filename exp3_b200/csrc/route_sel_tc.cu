@@ -14,11 +14,12 @@
 //     thread keeps its row's running max and sum, giving the row's log-sum-exp;
 //   column sums of the probabilities, in one of two ways:
 //   - a tile with at most two chunks (t <= 256, every tile of a 32K layer): pass 1 writes each
-//     logit back into its accumulator column (and dispersion_mean's sqrt(u) weight into the u
-//     column); both chunks stay resident in the two TMEM buffers, and once the row LSEs are
-//     known each warp sums its 32 rows of every column with a 5-round shuffle butterfly
-//     (32 columns per 31 shuffles), the four warps meeting in shared memory. No product runs
-//     twice;
+//     2^(logit - running max) back into its accumulator column (and dispersion_mean's sqrt(u)
+//     weight into the u column), keeping each 32-column slice's max; both chunks stay resident
+//     in the two TMEM buffers, and once the row LSEs are known a probability is one multiply by
+//     2^(slice max - LSE); each warp sums its 32 rows of every column with a 5-round shuffle
+//     butterfly (32 columns per 31 shuffles), the four warps meeting in shared memory. No
+//     product or exponential runs twice;
 //   - longer tiles: pass 2, transposed (TMEM lane = block): S^T = mean_K . Q^T (and
 //     var_K . (Q^2)^T); each thread owns one block and adds up its rows' probabilities (row
 //     LSEs from shared memory), so the column sums need no cross-thread reduction.
@@ -93,8 +94,10 @@ FPX_INLINE float sel_logit(float dot, float udot, float scale, float scale2) {
 
 }  // namespace
 
+// mean_balanced's CTA is small enough for two per SM (shared memory, TMEM): its registers are
+// held to that.
 template <int kSel>  // 0 mean_balanced, 1 cgf_mean, 2 dispersion_mean
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kSel == 0 ? 2 : 1)
     selector_route_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_mkh,
                              const __grid_constant__ CUtensorMap tm_mkl, const __grid_constant__ CUtensorMap tm_vkh,
                              const __grid_constant__ CUtensorMap tm_vkl, SelParams p, int *device_error) {
@@ -267,6 +270,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto grp_sync = [&]() { named_sync(2, 128); };  // group 0 only (the selection)
     // Pass 1: running max / sum of this half of row e (log2 units), 32 columns at a time.
     float m = -INFINITY, ssum = 0.f;
+    // Resident path: each slice's running max after it, so that the kept 2^(logit - max)
+    // become probabilities with one multiply once the row LSE is known.
+    float sm0 = -INFINITY, sm1 = -INFINITY, sm2 = -INFINITY, sm3 = -INFINITY;
+    auto slice_max = [&](int k) { return k == 0 ? sm0 : k == 1 ? sm1 : k == 2 ? sm2 : sm3; };
     for (int u = 0; u < chunks; ++u) {
       const int a = u & 1;
       if (ok) ok = mbar_wait_warp(&sh.acc_full[a], (u >> 1) & 1, abort);
@@ -289,20 +296,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             vl[c] = x;
             cmax = fmaxf(cmax, x);
           }
-          if (resident) {  // keep the logits (and weights) for the column sums
-            tmem_st32(tmem + lane_off + kAccStride * a + c0, vl);
-            if (kSel == 2) tmem_st32(tmem + lane_off + kAccStride * a + 128 + c0, vu);
-          }
           const float mn = fmaxf(m, cmax);
           if (mn != -INFINITY) {
             float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
             for (int c = 0; c < 32; c += 2) {
-              acc0 += ex2(vl[c] - mn);
-              acc1 += ex2(vl[c + 1] - mn);
+              const float e0 = ex2(vl[c] - mn), e1 = ex2(vl[c + 1] - mn);
+              acc0 += e0;
+              acc1 += e1;
+              vl[c] = e0;
+              vl[c + 1] = e1;
             }
             ssum = (m == -INFINITY ? 0.f : ssum * ex2(m - mn)) + (acc0 + acc1);
             m = mn;
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) vl[c] = 0.f;
+          }
+          if (resident) {  // keep 2^(logit - mn) (and the weights) for the column sums
+            tmem_st32(tmem + lane_off + kAccStride * a + c0, vl);
+            if (kSel == 2) tmem_st32(tmem + lane_off + kAccStride * a + 128 + c0, vu);
+            const int k = 2 * u + q2;
+            if (k == 0) sm0 = mn; else if (k == 1) sm1 = mn; else if (k == 2) sm2 = mn; else sm3 = mn;
           }
         }
       }
@@ -324,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       sh.lse[e] = mm + __log2f(s0 + s1);
     }
     all_sync();
-    // Resident path: p = 2^(logit - LSE) from the kept logits; warp ew sums its 32 rows of each
+    // Resident path: p = 2^(logit - LSE) from the kept exponentials; warp ew sums its 32 rows of each
     // 32-column slice by a shuffle butterfly (after the rounds lane l holds column l), the
     // four warps' partials meet in shared memory, and group 0 forms block kb = 128 c + e.
     for (int c = 0; resident && c < chunks; ++c) {
@@ -340,9 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tmem + lane_off + kAccStride * c + c0, v);
           if (kSel == 2) tmem_ld32(tmem + lane_off + kAccStride * c + 128 + c0, w);
           tmem_wait_ld();
+          // p = 2^(logit - mn) x 2^(mn - LSE); columns past the visible ones hold 0.
+          const float f = row_ok ? ex2(slice_max(2 * c + q2) - lse_row) : 0.f;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            float x = (row_ok && c0 + i < ncol) ? ex2(v[i] - lse_row) : 0.f;
+            float x = v[i] * f;
             if (kSel == 2) x *= w[i];
             v[i] = x;
           }
