@@ -1,9 +1,9 @@
 """Generate the golden vectors in this folder by running the exp3 reference itself.
 
-Run in the build container, where the reference tree is mounted (its path is
-the first argument, default ``/root/reference``); the GPU box never runs this.
+Run in the build container, where the reference tree is mounted; its path is the
+first argument (or ``FPX_REFERENCE_ROOT``). The GPU box never runs this.
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the reference tree>
 
 What runs, all on the CPU in fp32:
 - the reference's torch functions in ``kernels.py`` (descriptors, selectors,
@@ -103,7 +103,10 @@ def deal(upstream, score, alpha):
     return upstream._deal_output_score_compiled._torchdynamo_orig_callable(score, 2, 4, alpha, 2, 0)
 
 
-def main(root="/root/reference"):
+def main(root=None):
+    root = root or os.environ.get("FPX_REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("usage: make_golden.py <path of the reference tree> (or set FPX_REFERENCE_ROOT)")
     check_math, kernels, upstream = load_reference(root)
     torch.manual_seed(0)
 
